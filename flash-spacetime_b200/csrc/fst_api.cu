@@ -1,0 +1,131 @@
+// C-ABI front end of libflash_spacetime.so: argument validation, workspace
+// sizing, kernel selection and error reporting.
+//
+// Validation mirrors upstream's host checks (src/flash_spacetime/forward.py:
+// 258-265: channel/head-dim constraints), generalised to W = [Dh, C] with C
+// even. Errors are returned as status codes with a thread-local message; no
+// call traps or aborts.
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+#include <stdio.h>
+#include <string.h>
+
+#include "fst_internal.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int check_problem(const FstProblem* p) {
+  if (!p) return fail(FST_ERR_INVALID, "null problem");
+  if (p->dtype < FST_F32 || p->dtype > FST_F16)
+    return fail(FST_ERR_INVALID, "unknown dtype %d", p->dtype);
+  if (p->batch < 0 || p->heads <= 0 || p->head_dim <= 0 || p->channels <= 0)
+    return fail(FST_ERR_INVALID, "bad sizes B=%d H=%d Dh=%d C=%d", p->batch, p->heads,
+                p->head_dim, p->channels);
+  if (p->channels % 2)
+    return fail(FST_ERR_INVALID, "C (=%d) must be even (sin/cos halves)", p->channels);
+  if (p->head_dim > 64 || p->channels > 64)
+    return fail(FST_ERR_UNSUPPORTED, "Dh (=%d) and C (=%d) must be <= 64", p->head_dim,
+                p->channels);
+  if (p->feat_stride < 4) return fail(FST_ERR_INVALID, "feat_stride must be >= 4");
+  if (p->total_rows < 0) return fail(FST_ERR_INVALID, "negative total_rows");
+  if (p->packed) {
+    if (!p->cu_seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "packed needs cu_seqlens");
+  } else {
+    if (!p->seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "padded needs seqlens");
+    if ((int64_t)p->batch * p->max_len != p->total_rows)
+      return fail(FST_ERR_INVALID, "padded total_rows must equal B*L");
+  }
+  if (p->total_rows > 0 && (!p->feats || !p->freqs))
+    return fail(FST_ERR_INVALID, "feats and freqs are required");
+  if ((p->use_attn_bias || p->use_act_bias) && p->total_rows > 0 && !p->weight)
+    return fail(FST_ERR_INVALID, "weight is required when a bias term is on");
+  return FST_OK;
+}
+
+int cuda_status(const char* where) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FST_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
+  return FST_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int fst_abi_version(void) { return FST_ABI_VERSION; }
+
+size_t fst_forward_workspace_size(const FstProblem* prob) {
+  (void)prob;
+  return 0;
+}
+
+size_t fst_backward_workspace_size(const FstProblem* prob) {
+  if (check_problem(prob) != FST_OK) return 0;
+  return fst::simt::bwd_workspace(*prob);
+}
+
+int64_t fst_dw_partial_count(const FstProblem* prob) {
+  if (check_problem(prob) != FST_OK) return 0;
+  return fst::simt::dw_parts(*prob);
+}
+
+int fst_forward(const FstForwardArgs* a, void* stream) {
+  if (!a) return fail(FST_ERR_INVALID, "null args");
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  const FstProblem& p = a->prob;
+  if (p.total_rows > 0) {
+    if (!a->q || !a->k || !a->v || !a->out || !a->lse)
+      return fail(FST_ERR_INVALID, "forward: q, k, v, out and lse are required");
+    if (p.use_attn_bias && !a->u) return fail(FST_ERR_INVALID, "forward: u required (attn bias)");
+  }
+  cudaGetLastError();  // clear a stale error so the check below is ours
+  rc = fst::simt::launch_fwd(*a, (cudaStream_t)stream);
+  if (rc) return fail(rc, "forward launch failed");
+  return cuda_status("forward launch");
+}
+
+int fst_backward(const FstBackwardArgs* a, void* stream) {
+  if (!a) return fail(FST_ERR_INVALID, "null args");
+  int rc = check_problem(&a->prob);
+  if (rc) return rc;
+  const FstProblem& p = a->prob;
+  if (!a->dw_partial) return fail(FST_ERR_INVALID, "backward: dw_partial is required");
+  if (p.total_rows > 0) {
+    if (!a->q || !a->k || !a->v || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
+        !a->delta || !a->sigma)
+      return fail(FST_ERR_INVALID, "backward: a required pointer is null");
+    if (p.use_attn_bias && !a->u) return fail(FST_ERR_INVALID, "backward: u required");
+    if (p.use_act_bias && !a->wt) return fail(FST_ERR_INVALID, "backward: wt required");
+  }
+  const size_t need = fst_backward_workspace_size(&p);
+  if (need > 0 && (!a->workspace || a->workspace_bytes < need))
+    return fail(FST_ERR_WORKSPACE, "backward: workspace %zu bytes < required %zu",
+                a->workspace_bytes, need);
+  cudaGetLastError();
+  rc = fst::simt::launch_bwd(*a, (cudaStream_t)stream);
+  if (rc) return fail(rc, "backward launch failed");
+  return cuda_status("backward launch");
+}
+
+int fst_last_error(char* buf, size_t len) {
+  const int n = (int)strlen(g_err);
+  if (buf && len) {
+    strncpy(buf, g_err, len - 1);
+    buf[len - 1] = '\0';
+  }
+  return n;
+}
+
+}  // extern "C"

@@ -1,0 +1,107 @@
+// Shared device helpers for the fused spacetime-bias attention kernels.
+//
+// Layout addressing (padded [B,H,L,*] vs packed [T,H,*]), dtype conversion and
+// the pair angle x_ij of the spacetime interval. The angle follows upstream
+// src/flash_spacetime/_tiles.py:25-42 (itself the encoder definition of
+// reference.py:75-81): I = |dp|^2 - (dt * 18)^2, x = 1024 clip(sign(I)
+// sqrt|I|, -4, 4), with sign(0) = 0.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "../../include/flash_spacetime.h"
+
+namespace fst {
+
+constexpr float kTimeScale = 18.0f;    // 3e4 / 500 * 0.3, exact in fp32
+constexpr float kInputScale = 1024.0f;
+constexpr float kClip = 4.0f;
+constexpr float kLog2e = 1.4426950408889634f;
+
+template <typename T> __device__ __forceinline__ float to_f(T x);
+template <> __device__ __forceinline__ float to_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ float to_f<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+template <> __device__ __forceinline__ float to_f<__half>(__half x) { return __half2float(x); }
+
+template <typename T> __device__ __forceinline__ T from_f(float x);
+template <> __device__ __forceinline__ float from_f<float>(float x) { return x; }
+template <> __device__ __forceinline__ __nv_bfloat16 from_f<__nv_bfloat16>(float x) {
+  return __float2bfloat16_rn(x);
+}
+template <> __device__ __forceinline__ __half from_f<__half>(float x) {
+  return __float2half_rn(x);
+}
+
+// Where one event lives. `row0` is the flat row of the event's first token in
+// the [rows] index space (padded: b*L, packed: cu[b]); `len` its valid length.
+struct EventSpan {
+  int64_t row0;
+  int len;
+};
+
+__device__ __forceinline__ EventSpan event_span(const FstProblem& p, int b) {
+  EventSpan e;
+  if (p.packed) {
+    int s0 = p.cu_seqlens[b];
+    e.row0 = s0;
+    e.len = p.cu_seqlens[b + 1] - s0;
+  } else {
+    e.row0 = (int64_t)b * p.max_len;
+    e.len = p.seqlens[b];
+  }
+  return e;
+}
+
+// Event that owns packed row t: the largest b with cu[b] <= t (binary search).
+__device__ __forceinline__ int packed_event_of(const int32_t* cu, int batch, int64_t t) {
+  int lo = 0, hi = batch - 1;
+  while (lo < hi) {
+    int mid = (lo + hi + 1) >> 1;
+    if ((int64_t)cu[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+// Element offset of (row, head, 0) in a [*, H, D] (packed) or [B, H, L, D]
+// (padded) tensor, where `row` is a flat row index as in EventSpan.
+__device__ __forceinline__ int64_t vec_off(const FstProblem& p, int64_t row, int h, int dim) {
+  if (p.packed) return (row * p.heads + h) * (int64_t)dim;
+  int64_t b = row / p.max_len;
+  int64_t i = row - b * p.max_len;
+  return ((b * p.heads + h) * p.max_len + i) * (int64_t)dim;
+}
+
+// Offset of (row, head) in a per-row-per-head fp32 vector (LSE, D, sigma).
+__device__ __forceinline__ int64_t stat_off(const FstProblem& p, int64_t row, int h) {
+  return vec_off(p, row, h, 1);
+}
+
+struct Coord4 {
+  float x, y, z, t;
+};
+
+__device__ __forceinline__ Coord4 load_coord(const FstProblem& p, int64_t row) {
+  const float* f = p.feats + row * p.feat_stride;
+  Coord4 c;
+  c.x = f[0];
+  c.y = f[1];
+  c.z = f[2];
+  c.t = f[3];
+  return c;
+}
+
+// x_ij in fp32 (upstream _tiles.py:25-42).
+__device__ __forceinline__ float pair_angle(const Coord4& a, const Coord4& b) {
+  float dx = a.x - b.x, dy = a.y - b.y, dz = a.z - b.z;
+  float dt = (a.t - b.t) * kTimeScale;
+  float iv = dx * dx + dy * dy + dz * dz - dt * dt;
+  float d = iv > 0.f ? sqrtf(iv) : -sqrtf(-iv);
+  d = iv == 0.f ? 0.f : d;
+  return kInputScale * fminf(fmaxf(d, -kClip), kClip);
+}
+
+}  // namespace fst

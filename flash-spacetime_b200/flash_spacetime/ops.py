@@ -1,0 +1,431 @@
+"""Public ops and the autograd boundary of fused spacetime-bias attention.
+
+``flash_spacetime_attention`` (padded ``[B, H, L, Dh]``) and
+``flash_spacetime_attention_varlen`` (packed ``[T, H, Dh]`` with
+``cu_seqlens``) keep the upstream signatures (upstream
+src/flash_spacetime/forward.py:481-527). Behind them a single
+``torch.autograd.Function`` does what upstream's host drivers do on the
+host -- the float32 projection ``u = (q * scale) @ W`` of the queries through
+the encoder weight (forward.py:279-286), and ``w~ = dO @ W`` in the backward
+(backward.py:546-556) -- and calls the CUDA library through its C ABI
+(``_lib``). The output-side epilogues upstream also runs on the host
+(``A' W^T + b``, forward.py:333-345; ``dq``, backward.py:600-605) are fused
+into the kernels. There is no other code path: no Triton, no CPU fallback.
+
+Conventions kept from upstream:
+
+* the output has q's dtype and padding rows are exactly 0 (forward.py:19-22);
+* ``feats`` must not require grad (ValueError, forward.py:372-373);
+* ``dW``/``db`` are None when both bias terms are off, ``db`` is zeros when
+  only the logit term is on (forward.py:417-432, backward.py:615-622);
+* results are bitwise deterministic run to run.
+"""
+
+import ctypes
+from typing import Any, Dict, Optional, Tuple
+
+import torch
+from torch import Tensor
+
+from . import _lib
+from .reference import sinusoidal_frequencies
+
+_DTYPES = {
+    torch.float32: _lib.FST_F32,
+    torch.bfloat16: _lib.FST_BF16,
+    torch.float16: _lib.FST_F16,
+}
+
+_freq_cache: Dict[Tuple[int, str], Tensor] = {}
+
+
+def _freqs(channels: int, device: torch.device) -> Tensor:
+    """float32 frequency ladder, evaluated on the CPU once per (C, device).
+
+    Computing it on the CPU keeps the ladder bitwise identical to the CPU
+    oracle whatever device the op runs on.
+    """
+    key = (channels, str(device))
+    t = _freq_cache.get(key)
+    if t is None:
+        t = sinusoidal_frequencies(channels, torch.device("cpu")).to(device)
+        _freq_cache[key] = t
+    return t
+
+
+def _ptr(t: Optional[Tensor]) -> Optional[int]:
+    return None if t is None else t.data_ptr()
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def seqlens_from_mask(mask: Tensor, validate: bool = True) -> Tensor:
+    """Valid prefix lengths ``[B]`` from a ``[B, L]`` key-padding mask.
+
+    Accepts a bool mask (True = padding, the PyTorch ``key_padding_mask``
+    convention) or a float mask (0 valid / -inf padding, the ``Attention_rel``
+    convention of upstream reference.py:91-97). The fused op assumes
+    front-packed padding (upstream forward.py:241-242); with ``validate`` a
+    mask whose valid tokens are not a prefix raises ValueError (this check
+    reads one flag back from the device).
+    """
+    if mask.dim() != 2:
+        raise ValueError(f"key_padding_mask must be [B, L], got {tuple(mask.shape)}")
+    pad = mask if mask.dtype == torch.bool else torch.isneginf(mask)
+    valid = ~pad
+    lengths = valid.sum(1, dtype=torch.int32)
+    if validate:
+        pos = torch.arange(mask.shape[1], device=mask.device)
+        if not torch.equal(valid, pos[None, :] < lengths[:, None]):
+            raise ValueError(
+                "key_padding_mask must mark a prefix of each event as valid "
+                "(front-packed padding); reorder the tokens of each event"
+            )
+    return lengths
+
+
+class _Problem:
+    """Shapes and host-side tensors of one call, in C-ABI form."""
+
+    def __init__(
+        self,
+        q: Tensor,
+        feats: Tensor,
+        weight: Tensor,
+        bias: Optional[Tensor],
+        seqlens: Optional[Tensor],
+        cu_seqlens: Optional[Tensor],
+        scale: Optional[float],
+        use_attn_bias: bool,
+        use_act_bias: bool,
+    ) -> None:
+        self.packed = cu_seqlens is not None
+        if q.dtype not in _DTYPES:
+            raise ValueError(f"unsupported dtype {q.dtype}")
+        if not q.is_cuda:
+            raise ValueError("flash_spacetime runs on CUDA tensors only")
+        if self.packed:
+            if q.dim() != 3:
+                raise ValueError(f"varlen q must be [T, H, D], got {tuple(q.shape)}")
+            total, heads, dim = q.shape
+            self.cu = cu_seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+            batch = self.cu.numel() - 1
+            length = 0
+            self.seq = None
+            rows = total
+            if feats.dim() != 2 or feats.shape[0] != total:
+                raise ValueError(f"varlen feats must be [T, F], got {tuple(feats.shape)}")
+        else:
+            if q.dim() != 4:
+                raise ValueError(f"q must be [B, H, L, D], got {tuple(q.shape)}")
+            batch, heads, length, dim = q.shape
+            self.cu = None
+            self.seq = seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+            if self.seq.shape != (batch,):
+                raise ValueError(f"seqlens must be [B] = [{batch}], got {tuple(self.seq.shape)}")
+            rows = batch * length
+            if feats.dim() != 3 or feats.shape[:2] != (batch, length):
+                raise ValueError(f"feats must be [B, L, F], got {tuple(feats.shape)}")
+        if feats.shape[-1] < 4:
+            raise ValueError("feats needs at least 4 columns (x, y, z, t)")
+        if weight.dim() != 2 or weight.shape[0] != dim:
+            raise ValueError(
+                f"weight must be [head_dim, C] = [{dim}, C] (nn.Linear layout), "
+                f"got {tuple(weight.shape)}"
+            )
+        channels = weight.shape[1]
+        if channels % 2:
+            raise ValueError(f"C (={channels}) must be even")
+        if bias is not None and bias.shape != (dim,):
+            raise ValueError(f"bias must be [{dim}], got {tuple(bias.shape)}")
+        self.batch, self.heads, self.length, self.dim = batch, heads, length, dim
+        self.channels, self.rows = channels, rows
+        self.scale = float(dim**-0.5 if scale is None else scale)
+        self.attn, self.act = bool(use_attn_bias), bool(use_act_bias)
+        self.dtype = q.dtype
+        self.device = q.device
+        self.feats = feats[..., :4].to(torch.float32).contiguous()
+        self.freqs = _freqs(channels, q.device)
+        self.w32 = weight.detach().to(torch.float32).contiguous()
+        self.b32 = None if bias is None else bias.detach().to(torch.float32).contiguous()
+
+    def c_struct(self) -> _lib.FstProblem:
+        p = _lib.FstProblem()
+        p.dtype = _DTYPES[self.dtype]
+        p.packed = int(self.packed)
+        p.batch = self.batch
+        p.heads = self.heads
+        p.max_len = self.length
+        p.head_dim = self.dim
+        p.channels = self.channels
+        p.feat_stride = 4
+        p.total_rows = self.rows
+        p.scale = self.scale
+        p.use_attn_bias = int(self.attn)
+        p.use_act_bias = int(self.act)
+        p.seqlens = _ptr(self.seq)
+        p.cu_seqlens = _ptr(self.cu)
+        p.feats = _ptr(self.feats)
+        p.freqs = _ptr(self.freqs)
+        p.weight = _ptr(self.w32)
+        p.bias = _ptr(self.b32)
+        return p
+
+    def stat_shape(self) -> Tuple[int, ...]:
+        if self.packed:
+            return (self.rows, self.heads)
+        return (self.batch, self.heads, self.length)
+
+    def project_queries(self, q: Tensor) -> Optional[Tensor]:
+        """``u = (q * scale) @ W`` in fp32, rounded to q's dtype (forward.py:279-286)."""
+        if not self.attn:
+            return None
+        return ((q.to(torch.float32) * self.scale) @ self.w32).to(q.dtype).contiguous()
+
+    def valid_rows(self) -> Optional[Tensor]:
+        """``[B, 1, L, 1]`` bool of valid rows (padded layout), else None."""
+        if self.packed:
+            return None
+        pos = torch.arange(self.length, device=self.device)
+        return (pos[None, :] < self.seq[:, None])[:, None, :, None]
+
+
+def _workspace(nbytes: int, device: torch.device) -> Tuple[Optional[Tensor], int]:
+    if nbytes == 0:
+        return None, 0
+    return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
+
+
+def fused_forward(pb: _Problem, q: Tensor, k: Tensor, v: Tensor) -> Tuple[Tensor, Tensor]:
+    """One ``fst_forward`` call. Returns ``(out, lse)``."""
+    lib = _lib.load()
+    u = pb.project_queries(q)
+    out = torch.empty_like(q)
+    lse = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
+    a = _lib.FstForwardArgs()
+    a.prob = pb.c_struct()
+    ws, nws = _workspace(lib.fst_forward_workspace_size(ctypes.byref(a.prob)), pb.device)
+    a.q, a.k, a.v, a.u = _ptr(q), _ptr(k), _ptr(v), _ptr(u)
+    a.out, a.lse = _ptr(out), _ptr(lse)
+    a.workspace, a.workspace_bytes = _ptr(ws), nws
+    _lib.check(lib.fst_forward(ctypes.byref(a), _stream(pb.device)), "fst_forward")
+    return out, lse
+
+
+def fused_backward(
+    pb: _Problem,
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    out: Tensor,
+    lse: Tensor,
+    dout: Tensor,
+    want_absmax: bool = False,
+) -> Dict[str, Optional[Tensor]]:
+    """One ``fst_backward`` call plus the two deterministic host reductions.
+
+    Returns dq, dk, dv (input dtype), dW ``[Dh, C]`` and db ``[Dh]`` (fp32,
+    or None when the projection is unused), and the per-row diagnostics
+    delta (D), sigma (rowsum dS) and, on request, rowmax |dS|.
+    """
+    lib = _lib.load()
+    dout = dout.contiguous()
+    u = pb.project_queries(q)
+    wt = None
+    if pb.act:
+        wt = (dout.to(torch.float32) @ pb.w32).to(dout.dtype).contiguous()
+    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    a = _lib.FstBackwardArgs()
+    a.prob = pb.c_struct()
+    nparts = int(lib.fst_dw_partial_count(ctypes.byref(a.prob)))
+    dw_part = torch.empty(max(nparts, 1), pb.dim, pb.channels, dtype=torch.float32,
+                          device=pb.device)
+    delta = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
+    sigma = torch.empty_like(delta)
+    absmax = torch.empty_like(delta) if want_absmax else None
+    ws, nws = _workspace(lib.fst_backward_workspace_size(ctypes.byref(a.prob)), pb.device)
+    a.q, a.k, a.v, a.u, a.out = _ptr(q), _ptr(k), _ptr(v), _ptr(u), _ptr(out)
+    a.dout, a.wt, a.lse = _ptr(dout), _ptr(wt), _ptr(lse)
+    a.dq, a.dk, a.dv = _ptr(dq), _ptr(dk), _ptr(dv)
+    a.dw_partial, a.delta, a.sigma = _ptr(dw_part), _ptr(delta), _ptr(sigma)
+    a.ds_absmax = _ptr(absmax)
+    a.workspace, a.workspace_bytes = _ptr(ws), nws
+    _lib.check(lib.fst_backward(ctypes.byref(a), _stream(pb.device)), "fst_backward")
+
+    dw = db = None
+    if pb.attn or pb.act:
+        dw = dw_part[:nparts].sum(0)
+    if pb.b32 is not None:
+        if pb.act:
+            rows = dout.to(torch.float32)
+            valid = pb.valid_rows()
+            if valid is not None:
+                rows = torch.where(valid, rows, torch.zeros((), device=pb.device))
+            db = rows.reshape(-1, pb.dim).sum(0)
+        else:
+            db = torch.zeros(pb.dim, dtype=torch.float32, device=pb.device)
+    return {"dq": dq, "dk": dk, "dv": dv, "dW": dw, "db": db,
+            "delta": delta, "sigma": sigma, "ds_absmax": absmax}
+
+
+class _FlashSpacetimeAttention(torch.autograd.Function):
+    """Fused forward and deterministic fused backward (upstream forward.py:349-478)."""
+
+    @staticmethod
+    def forward(  # type: ignore[override]
+        ctx: Any,
+        q: Tensor,
+        k: Tensor,
+        v: Tensor,
+        feats: Tensor,
+        weight: Tensor,
+        bias: Optional[Tensor],
+        seqlens: Optional[Tensor],
+        cu_seqlens: Optional[Tensor],
+        scale: Optional[float],
+        use_attn_bias: bool,
+        use_activation_bias: bool,
+    ) -> Tensor:
+        if feats.requires_grad:
+            raise ValueError("feats (detector data) must not require grad")
+        if k.shape != q.shape or v.shape != q.shape:
+            raise ValueError("q, k and v must have the same shape")
+        if k.dtype != q.dtype or v.dtype != q.dtype:
+            raise ValueError("q, k and v must have the same dtype")
+        pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
+                      use_attn_bias, use_activation_bias)
+        qc, kc, vc = (t.contiguous() for t in (q, k, v))
+        out, lse = fused_forward(pb, qc, kc, vc)
+        ctx.save_for_backward(qc, kc, vc, out, lse)
+        ctx.pb = pb
+        ctx.weight_dtype = weight.dtype
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, grad_out: Tensor) -> Tuple[Optional[Tensor], ...]:  # type: ignore[override]
+        q, k, v, out, lse = ctx.saved_tensors
+        pb: _Problem = ctx.pb
+        g = fused_backward(pb, q, k, v, out, lse, grad_out)
+        proj_used = pb.attn or pb.act
+        need = ctx.needs_input_grad
+        dw = g["dW"].to(ctx.weight_dtype) if (proj_used and need[4]) else None
+        db = None
+        if ctx.bias_dtype is not None and proj_used and need[5]:
+            db = g["db"].to(ctx.bias_dtype)
+        return (
+            g["dq"] if need[0] else None,
+            g["dk"] if need[1] else None,
+            g["dv"] if need[2] else None,
+            None, dw, db, None, None, None, None, None,
+        )
+
+
+def flash_spacetime_attention(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    seqlens: Optional[Tensor] = None,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+    *,
+    key_padding_mask: Optional[Tensor] = None,
+) -> Tensor:
+    """Fused spacetime-bias attention on a padded batch (upstream forward.py:481-501).
+
+    q, k, v: ``[B, H, L, Dh]`` (fp32, bf16 or fp16). feats: ``[B, L, F]`` with
+    x, y, z in columns 0-2 and time in column 3. weight: ``[Dh, C]``; bias:
+    ``[Dh]`` or None. The 7th argument takes the ``[B]`` valid lengths
+    (upstream's form); a ``[B, L]`` key-padding mask, bool (True = padding)
+    or float (0 / -inf), is accepted there or as ``key_padding_mask=``.
+    Returns ``[B, H, L, Dh]`` in q's dtype with padding rows exactly 0.
+    """
+    if key_padding_mask is not None:
+        if seqlens is not None:
+            raise ValueError("pass seqlens or key_padding_mask, not both")
+        seqlens = seqlens_from_mask(key_padding_mask)
+    elif seqlens is None:
+        seqlens = torch.full((q.shape[0],), q.shape[2], dtype=torch.int32, device=q.device)
+    elif seqlens.dim() == 2:
+        seqlens = seqlens_from_mask(seqlens)
+    return _FlashSpacetimeAttention.apply(
+        q, k, v, feats, weight, bias, seqlens, None,
+        scale, use_attn_bias, use_activation_bias,
+    )
+
+
+def flash_spacetime_attention_varlen(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    cu_seqlens: Tensor,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+) -> Tensor:
+    """Packed, uncapped variant (upstream forward.py:504-527).
+
+    q, k, v: ``[T, H, Dh]``; feats ``[T, F]``; ``cu_seqlens`` ``[B+1]`` token
+    offsets (cu[0] = 0, cu[-1] = T) -- the values buffer of a jagged
+    NestedTensor. No padding exists and no host synchronisation happens.
+    """
+    return _FlashSpacetimeAttention.apply(
+        q, k, v, feats, weight, bias, None, cu_seqlens,
+        scale, use_attn_bias, use_activation_bias,
+    )
+
+
+def flash_spacetime_forward(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    seqlens: Optional[Tensor],
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+    cu_seqlens: Optional[Tensor] = None,
+) -> Tuple[Tensor, Tensor]:
+    """Forward only, returning ``(out, lse)`` (upstream forward.py:222-346)."""
+    pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
+                  use_attn_bias, use_activation_bias)
+    return fused_forward(pb, q.contiguous(), k.contiguous(), v.contiguous())
+
+
+def flash_spacetime_backward(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    seqlens: Optional[Tensor],
+    out: Tensor,
+    lse: Tensor,
+    grad_out: Tensor,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+    cu_seqlens: Optional[Tensor] = None,
+    want_absmax: bool = False,
+) -> Dict[str, Optional[Tensor]]:
+    """Backward only (upstream backward.py:488-630), with diagnostics.
+
+    Returns dq, dk, dv, dW, db plus ``delta`` (D), ``sigma`` (rowsum dS, zero
+    by construction) and, with ``want_absmax``, ``ds_absmax`` (rowmax |dS|).
+    """
+    pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
+                  use_attn_bias, use_activation_bias)
+    return fused_backward(pb, q.contiguous(), k.contiguous(), v.contiguous(),
+                          out, lse, grad_out, want_absmax)

@@ -1,0 +1,152 @@
+/*
+ * flash_spacetime.h -- C ABI of the B200 (sm_100a) fused spacetime-bias
+ * attention library (libflash_spacetime.so).
+ *
+ * The library computes, per event and head,
+ *
+ *   s_ij  = qt_i . k_j + [attn] u_i . E_ij          (qt = q * scale, u = qt W)
+ *   P     = softmax_j(s)
+ *   out_i = sum_j P_ij v_j + [act] (sum_j P_ij E_ij) W^T + b
+ *
+ * with E_ij the C-channel sinusoidal embedding of the clipped, signed
+ * spacetime interval between pulses i and j, and its gradients. It replaces
+ * the Triton launches of the upstream package:
+ *
+ *   fst_forward   <- flash_spacetime_fwd_kernel launch and the host epilogue
+ *                    of flash_spacetime_forward
+ *                    (upstream src/flash_spacetime/forward.py:222-346,
+ *                    kernel forward.py:63-219)
+ *   fst_backward  <- flash_spacetime_bwd_rows_kernel + _cols_kernel launches
+ *                    and the dq/dW epilogue of flash_spacetime_backward
+ *                    (upstream src/flash_spacetime/backward.py:488-630,
+ *                    kernels backward.py:209-485)
+ *
+ * Everything is plain C: raw device pointers, sizes and a cudaStream_t passed
+ * as void*. The caller (the PyTorch autograd Function in flash_spacetime/ops.py,
+ * or any other host) owns every buffer; the library allocates no device
+ * memory. Calls are stream-ordered and asynchronous; a non-zero return is an
+ * error whose text fst_last_error() returns (thread-local).
+ *
+ * Layouts (contiguous, row-major):
+ *   padded (packed == 0): q,k,v,u,out,dout,wt [B, H, L, D*] ; feats [B, L, fs]
+ *                         lse/delta/sigma [B, H, L] ; rows i >= seqlens[b] are
+ *                         padding and every per-row output there is written 0.
+ *   packed (packed == 1): q,k,v,u,out,dout,wt [T, H, D*] ; feats [T, fs]
+ *                         lse/delta/sigma [T, H] ; event b is rows
+ *                         [cu_seqlens[b], cu_seqlens[b+1]).
+ * D* is Dh for q,k,v,out,dout and C for u, wt.
+ */
+#ifndef FLASH_SPACETIME_H_
+#define FLASH_SPACETIME_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FST_ABI_VERSION 1
+
+/* Storage dtype of q, k, v, u, wt, out, dout, dq, dk, dv. */
+enum FstDtype { FST_F32 = 0, FST_BF16 = 1, FST_F16 = 2 };
+
+/* Return codes. */
+enum FstStatus {
+  FST_OK = 0,
+  FST_ERR_INVALID = 1,     /* bad shape / pointer / flag combination        */
+  FST_ERR_UNSUPPORTED = 2, /* valid request this build does not implement   */
+  FST_ERR_CUDA = 3,        /* a CUDA runtime call failed                    */
+  FST_ERR_WORKSPACE = 4,   /* workspace pointer NULL or too small           */
+  FST_ERR_DEVICE = 5       /* the device reported a failed self-check       */
+};
+
+/*
+ * Problem description shared by forward and backward.
+ * Mirrors the arguments of upstream flash_spacetime_forward
+ * (forward.py:222-237): q/k/v shapes, weight [Dh, C], bias [Dh], seqlens or
+ * cu_seqlens, scale, use_attn_bias, use_activation_bias.
+ */
+typedef struct FstProblem {
+  int32_t dtype;          /* enum FstDtype                                   */
+  int32_t packed;         /* 0 padded [B,H,L,*], 1 packed [T,H,*]            */
+  int32_t batch;          /* B: number of events                             */
+  int32_t heads;          /* H                                               */
+  int32_t max_len;        /* padded: L. packed: an upper bound on any event  */
+                          /* length, or 0 if unknown                         */
+  int32_t head_dim;       /* Dh                                              */
+  int32_t channels;       /* C: embedding channels, even                     */
+  int32_t feat_stride;    /* floats between consecutive feats rows (>= 4)    */
+  int64_t total_rows;     /* padded: B*L. packed: T                          */
+  float scale;            /* query scale (Dh^-0.5 by default)                */
+  int32_t use_attn_bias;  /* add u_i . E_ij to the logits                    */
+  int32_t use_act_bias;   /* add (sum_j P_ij E_ij) W^T + b to the output     */
+  const int32_t* seqlens;    /* [B] device, valid prefix lengths (padded)     */
+  const int32_t* cu_seqlens; /* [B+1] device token offsets (packed)           */
+  const float* feats;        /* device fp32: x, y, z in cols 0-2, time col 3  */
+  const float* freqs;        /* [C/2] device fp32 frequency ladder            */
+  const float* weight;       /* [Dh, C] device fp32 (nn.Linear layout)        */
+  const float* bias;         /* [Dh] device fp32, or NULL                     */
+} FstProblem;
+
+typedef struct FstForwardArgs {
+  FstProblem prob;
+  const void* q;         /* unscaled queries                                 */
+  const void* k;
+  const void* v;
+  const void* u;         /* (q*scale) @ W rounded to dtype; NULL if !attn    */
+  void* out;             /* output, same layout/dtype as q                   */
+  float* lse;            /* log-sum-exp of the logits WITHOUT the qt.b term  */
+  void* workspace;       /* device scratch, >= fst_forward_workspace_size()  */
+  size_t workspace_bytes;
+} FstForwardArgs;
+
+typedef struct FstBackwardArgs {
+  FstProblem prob;
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* u;         /* as in the forward; NULL if !attn                 */
+  const void* out;       /* forward output; gives the row offset dO.(out-b)  */
+                         /* subtracted from dP before summing. May be NULL. */
+  const void* dout;      /* upstream gradient, padding rows ignored          */
+  const void* wt;        /* dout @ W rounded to dtype; NULL if !act          */
+  const float* lse;      /* from fst_forward                                 */
+  void* dq;              /* outputs, layout/dtype of q                       */
+  void* dk;
+  void* dv;
+  float* dw_partial;     /* [fst_dw_partial_count(), Dh, C] fp32; the caller */
+                         /* sums axis 0 (fixed order) to obtain dW           */
+  float* delta;          /* [rows, H] fp32: D_i = sum P dP / sum P, dP taken */
+                         /* without its dO.b row constant (it cancels)       */
+  float* sigma;          /* [rows, H] fp32: rowsum(dS), zero by construction */
+  float* ds_absmax;      /* [rows, H] fp32: rowmax |dS|, or NULL             */
+  void* workspace;       /* device scratch, >= fst_backward_workspace_size() */
+  size_t workspace_bytes;
+} FstBackwardArgs;
+
+/* ABI version of the loaded library (FST_ABI_VERSION). */
+int fst_abi_version(void);
+
+/* Bytes of device scratch fst_forward / fst_backward need for this problem. */
+size_t fst_forward_workspace_size(const FstProblem* prob);
+size_t fst_backward_workspace_size(const FstProblem* prob);
+
+/* Rows of dw_partial fst_backward writes for this problem. */
+int64_t fst_dw_partial_count(const FstProblem* prob);
+
+/* Fused forward (upstream forward.py:222-346). */
+int fst_forward(const FstForwardArgs* args, void* stream);
+
+/* Fused backward (upstream backward.py:488-630). */
+int fst_backward(const FstBackwardArgs* args, void* stream);
+
+/* Copies the calling thread's last error message into buf (NUL-terminated).
+ * Returns the message length. */
+int fst_last_error(char* buf, size_t len);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASH_SPACETIME_H_ */

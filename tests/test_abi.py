@@ -1,0 +1,72 @@
+"""CPU checks of the C-ABI boundary: the library loads, exports every entry
+point declared in include/flash_spacetime.h, and the ctypes mirrors of the
+structs have the C layout (checked against gcc on the header itself)."""
+
+import ctypes
+import os
+import re
+import shutil
+import subprocess
+import tempfile
+
+import pytest
+
+from flash_spacetime import _lib
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+HEADER = os.path.join(ROOT, "include", "flash_spacetime.h")
+
+
+def _declared_functions():
+    text = open(HEADER).read()
+    return sorted(set(re.findall(r"^\w[\w\s\*]*?\b(fst_\w+)\s*\(", text, re.M)))
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    declared = _declared_functions()
+    assert declared, "no declarations found in the header"
+    assert set(declared) == set(_lib.EXPORTED)
+    for name in declared:
+        assert hasattr(lib, name), f"{name} declared in the header but not exported"
+    assert lib.fst_abi_version() == _lib.ABI_VERSION
+
+
+def test_invalid_problem_reports_error():
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.batch, p.heads, p.head_dim, p.channels = 1, 1, 1, 32, 15  # odd C
+    p.feat_stride = 4
+    a = _lib.FstForwardArgs()
+    a.prob = p
+    rc = lib.fst_forward(ctypes.byref(a), None)
+    assert rc == _lib.FST_ERR_INVALID
+    assert "even" in _lib.last_error()
+    with pytest.raises(ValueError):
+        _lib.check(rc, "fst_forward")
+
+
+@pytest.mark.skipif(shutil.which("gcc") is None, reason="needs gcc")
+def test_struct_layout_matches_header():
+    structs = {
+        "FstProblem": _lib.FstProblem,
+        "FstForwardArgs": _lib.FstForwardArgs,
+        "FstBackwardArgs": _lib.FstBackwardArgs,
+    }
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "flash_spacetime.h"',
+             "int main(void) {"]
+    for name, cls in structs.items():
+        lines.append(f'printf("{name} %zu\\n", sizeof({name}));')
+        for field, _ in cls._fields_:
+            lines.append(f'printf("{name}.{field} %zu\\n", offsetof({name}, {field}));')
+    lines += ["return 0;", "}"]
+    with tempfile.TemporaryDirectory() as tmp:
+        src, exe = os.path.join(tmp, "layout.c"), os.path.join(tmp, "layout")
+        open(src, "w").write("\n".join(lines))
+        subprocess.check_call(["gcc", "-I", os.path.dirname(HEADER), src, "-o", exe])
+        out = subprocess.check_output([exe]).decode().split("\n")
+    got = dict(line.split() for line in out if line.strip())
+    for name, cls in structs.items():
+        assert int(got[name]) == ctypes.sizeof(cls), name
+        for field, _ in cls._fields_:
+            assert int(got[f"{name}.{field}"]) == getattr(cls, field).offset, f"{name}.{field}"

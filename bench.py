@@ -1,0 +1,388 @@
+#!/usr/bin/env python
+"""Benchmark of the fused spacetime-bias attention op (fwd + bwd) on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload config1|config3|config4] [--coords raw|scaled]
+
+One step is one forward + backward of the op through its public API
+(``flash_spacetime_attention`` / ``..._varlen``) over one batch of seeded
+synthetic events. The default workload is configuration 1 of the baseline:
+B=256 events padded to L=768, H=12, Dh=32, C=16, bf16, lognormal lengths
+(median 120, sigma 1.2 -- the sigma the baseline leaves open -- clipped to
+[1, 768]). Throughput is algorithmic TFLOP/s over VALID pairs,
+sum_b L_b^2 * H * (14 Dh + 12 C).
+
+Under torchrun (N > 1) every rank owns a shard of N x 256 events chosen by
+longest-first L^2 balancing (weak scaling: per-GPU work stays fixed); the
+per-rank dW/db partials are gathered and summed in rank order (NCCL) inside
+the step, and the step time is the max over ranks of the device-timed
+duration.
+
+Printed: one JSON line on rank 0 (see the keys below). ``value`` has inputs
+resident in HBM; ``e2e`` repeats the step with the inputs copied from pinned
+host memory and dW read back every step. ``--impl reference`` times the CPU
+restatement of the upstream eager path (oracle/) on the host cores.
+"""
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for _p in (os.path.join(ROOT, "flash-spacetime_b200"), ROOT):
+    if _p not in sys.path:
+        sys.path.insert(0, _p)
+
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+HEADS, DIM, CHANNELS = 12, 32, 16
+METRIC = "fwd+bwd TFLOP/s (B=256,L=768,H=12,Dh=32,C=16 bf16; valid pairs)"
+
+
+def _peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            d = json.load(f)
+        return {"bf16_tflops": float(d["bf16_tflops"]), "hbm_gbs": float(d["hbm_gbs"]),
+                "src": "measured"}
+    except Exception:
+        return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def _dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def _workload_lengths(name: str, world: int, rank: int, seed: int):
+    """(all lengths of this rank's shard, padded length or None, global event count)."""
+    from flash_spacetime.sharding import lpt_partition
+    from flash_spacetime.synthetic import lengths_for
+
+    if name == "config1":
+        n = 256 * world
+        lens = lengths_for("config1", n, seed)
+        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(n))
+        return [lens[i] for i in shard], 768, n
+    if name == "config3":
+        lens = lengths_for("config3", 16384 * world, seed)
+        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(len(lens)))
+        return [lens[i] for i in shard], None, len(lens)
+    if name == "config4":
+        lens = lengths_for("config4", 2048, seed)  # fixed total: strong scaling
+        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(len(lens)))
+        return [lens[i] for i in shard], None, len(lens)
+    raise SystemExit(f"unknown workload {name}")
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except Exception:
+            self.proc.kill()
+            out = ""
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in out.strip().splitlines():
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sm.append(float(parts[0]))
+                smax.append(float(parts[1]))
+            except ValueError:
+                continue
+            for nm, flag in zip(names, parts[4:8]):
+                if flag.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+def cpu_eager_sample(lengths, budget_s: float, seed: int):
+    """Time the CPU restatement of the upstream eager op, event by event.
+
+    Runs fp32 forward + backward through autograd (upstream
+    src/flash_spacetime/reference.py:106-167) on events of the workload in
+    their natural order until ``budget_s`` seconds are spent; returns the
+    achieved algorithmic TFLOP/s over the events done.
+    """
+    from oracle.spacetime_oracle import eager_fwd_bwd_fp32
+    from flash_spacetime.synthetic import detector_coords, projection
+
+    gen = torch.Generator().manual_seed(seed)
+    proj = projection(DIM, CHANNELS, gen)
+    done_flops = 0.0
+    done_pairs = 0
+    spent = 0.0
+    events = 0
+    for n in lengths:
+        n = int(n)
+        feats = detector_coords([n], gen).view(1, n, 4)
+        q, k, v = (torch.randn(1, HEADS, n, DIM, generator=gen) for _ in range(3))
+        t0 = time.perf_counter()
+        eager_fwd_bwd_fp32(q, k, v, feats, proj["weight"], proj["bias"], None)
+        spent += time.perf_counter() - t0
+        done_flops += n * n * HEADS * (14 * DIM + 12 * CHANNELS)
+        done_pairs += n * n
+        events += 1
+        if spent >= budget_s:
+            break
+    return {"tflops": done_flops / spent / 1e12 if spent > 0 else 0.0, "seconds": spent,
+            "events": events, "pairs": done_pairs}
+
+
+def run_reference(args):
+    world, rank, _ = _dist_setup()
+    if rank != 0:
+        return
+    torch.set_num_threads(os.cpu_count() or 1)
+    lens, _, _ = _workload_lengths(args.workload, 1, 0, args.seed)
+    # Each step: a bounded sample of the workload's events (in order).
+    for _ in range(args.warmup):
+        cpu_eager_sample(lens, 0.5, args.seed)
+    vals, secs = [], []
+    sample = None
+    for _ in range(args.steps):
+        sample = cpu_eager_sample(lens, args.ref_budget, args.seed)
+        vals.append(sample["tflops"])
+        secs.append(sample["seconds"])
+    value = statistics.median(vals)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.median(secs), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
+        "config": {"workload": args.workload, "events_per_step": sample["events"],
+                   "pairs_per_step": sample["pairs"]},
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+                         "kind": "port",
+                         "sample": f"first {sample['events']} events of {args.workload}, "
+                                   "one event at a time, fp32 eager fwd+bwd via autograd"},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args):
+    world, rank, local = _dist_setup()
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=device,
+                                timeout=__import__("datetime").timedelta(seconds=120))
+    from flash_spacetime import _lib, ops, synthetic
+    from flash_spacetime.sharding import max_over_ranks, ordered_sum
+
+    lens, padlen, n_events = _workload_lengths(args.workload, world, rank, args.seed)
+    dtype = torch.bfloat16
+    scaled = args.coords == "scaled"
+    if padlen is not None:
+        data = synthetic.padded_batch(lens, padlen, HEADS, DIM, CHANNELS, dtype, device,
+                                      args.seed + 17 * rank, scaled)
+    else:
+        data = synthetic.packed_batch(lens, HEADS, DIM, CHANNELS, dtype, device,
+                                      args.seed + 17 * rank, scaled)
+    flops = synthetic.pair_flops(lens, HEADS, DIM, CHANNELS)
+
+    leaves = {k: data[k].detach().clone().requires_grad_(True)
+              for k in ("q", "k", "v", "weight", "bias")}
+    grad = data["grad"]
+    feats = data["feats"]
+
+    def step(lv, feats_, grad_, seq_or_cu):
+        for t in lv.values():
+            t.grad = None
+        if padlen is not None:
+            out = ops.flash_spacetime_attention(lv["q"], lv["k"], lv["v"], feats_, lv["weight"],
+                                                lv["bias"], seq_or_cu)
+        else:
+            out = ops.flash_spacetime_attention_varlen(lv["q"], lv["k"], lv["v"], feats_,
+                                                       lv["weight"], lv["bias"], seq_or_cu)
+        out.backward(grad_)
+        dw = lv["weight"].grad
+        db = lv["bias"].grad
+        if world > 1:
+            flat = torch.cat([dw.flatten(), db.flatten()])
+            flat = ordered_sum(flat)
+            dw = flat[: dw.numel()].view_as(dw)
+            db = flat[dw.numel():]
+        return out, dw, db
+
+    index = data["seqlens"] if padlen is not None else data["cu_seqlens"]
+    timers = []
+    ops.set_kernel_timer(timers)
+    for _ in range(args.warmup):
+        step(leaves, feats, grad, index)
+    torch.cuda.synchronize()
+    timers.clear()
+
+    torch.cuda.reset_peak_memory_stats(device)
+    base_mem = torch.cuda.memory_allocated(device)
+    lib = _lib.load()
+    launches0 = lib.fst_kernel_launches()
+    clocks = ClockSampler(local)
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    ev0.record()
+    for _ in range(args.steps):
+        step(leaves, feats, grad, index)
+    ev1.record()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    clk = clocks.stop()
+    launches = lib.fst_kernel_launches() - launches0
+    ms_local = ev0.elapsed_time(ev1) / args.steps
+    ms = max_over_ranks(ms_local, device)
+    peak_gib = (torch.cuda.max_memory_allocated(device) - base_mem) / 2**30
+    ops.set_kernel_timer(None)
+
+    # Per-kernel device times inside the timed steps.
+    per = {}
+    for name, e0, e1 in timers:
+        per.setdefault(name, []).append(e0.elapsed_time(e1))
+    fwd_ms = statistics.mean(per.get("fst_forward", [0.0]))
+    bwd_ms = statistics.mean(per.get("fst_backward", [0.0]))
+    total_flops = flops["total"] * world
+    value = total_flops / (ms * 1e-3) / 1e12
+
+    # End to end: inputs from pinned host memory every step, dW read back.
+    host = {k: data[k].detach().cpu().pin_memory() for k in ("q", "k", "v", "grad", "feats")}
+    host_index = index.cpu().pin_memory()
+    host_w = {k: data[k].detach().cpu().pin_memory() for k in ("weight", "bias")}
+    h2d = sum(t.numel() * t.element_size() for t in list(host.values()) + [host_index]
+              + list(host_w.values()))
+    dw_host = torch.empty(DIM * CHANNELS + DIM, dtype=torch.float32).pin_memory()
+    d2h = dw_host.numel() * dw_host.element_size()
+
+    def e2e_step():
+        dev = {k: t.to(device, non_blocking=True) for k, t in host.items()}
+        lv = {k: t.to(device, non_blocking=True) for k, t in host_w.items()}
+        for k in ("q", "k", "v"):
+            lv[k] = dev[k]
+        for t in lv.values():
+            t.requires_grad_(True)
+        idx = host_index.to(device, non_blocking=True)
+        _, dw, db = step(lv, dev["feats"], dev["grad"], idx)
+        dw_host.copy_(torch.cat([dw.flatten().float(), db.flatten().float()]), non_blocking=True)
+
+    for _ in range(max(1, args.warmup)):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        e2e_step()
+    e1.record()
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, device)
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+
+    peaks = _peaks()
+    dom = "fst_backward" if bwd_ms >= fwd_ms else "fst_forward"
+    dom_ms = bwd_ms if dom == "fst_backward" else fwd_ms
+    dom_flops = flops["bwd"] if dom == "fst_backward" else flops["fwd"]
+    achieved = dom_flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 0 else 0.0
+
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        torch.set_num_threads(os.cpu_count() or 1)
+        s = cpu_eager_sample(lens, args.cpu_budget, args.seed)
+        cpu = {"value": s["tflops"], "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+               "kind": "port",
+               "sample": f"first {s['events']} events ({s['pairs']} valid pairs) of "
+                         f"{args.workload}, one event at a time, fp32 eager fwd+bwd via "
+                         f"autograd, {s['seconds']:.1f} s"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
+        "higher_is_better": True, "scaling": "weak" if args.workload != "config4" else "strong",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": args.workload, "events": n_events, "heads": HEADS,
+                   "head_dim": DIM, "channels": CHANNELS,
+                   "padded_length": padlen, "coords": args.coords,
+                   "valid_pairs_per_gpu": flops["pairs"],
+                   "l2_policy": "inputs larger than L2 (q, k, v, grad 151 MB each)"},
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "peak_gib": peak_gib,
+        "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
+                     "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                     "peak_src": peaks["src"] + " burst bf16"},
+        "cpu_baseline": cpu,
+        "clocks": clk,
+        "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": launches,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--workload", default="config1", choices=("config1", "config3", "config4"))
+    ap.add_argument("--coords", default="raw", choices=("raw", "scaled"))
+    ap.add_argument("--seed", type=int, default=2026)
+    ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--ref-budget", type=float, default=6.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

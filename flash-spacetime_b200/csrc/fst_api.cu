@@ -11,7 +11,14 @@
 #include <stdio.h>
 #include <string.h>
 
+#include <atomic>
+
 #include "fst_internal.h"
+
+namespace fst {
+static std::atomic<int64_t> g_launches{0};
+void count_launch(int n) { g_launches.fetch_add(n, std::memory_order_relaxed); }
+}  // namespace fst
 
 namespace {
 
@@ -66,8 +73,8 @@ extern "C" {
 int fst_abi_version(void) { return FST_ABI_VERSION; }
 
 size_t fst_forward_workspace_size(const FstProblem* prob) {
-  (void)prob;
-  return 0;
+  if (check_problem(prob) != FST_OK) return 0;
+  return fst::tc::fwd_supported(*prob) ? fst::tc::fwd_workspace(*prob) : 0;
 }
 
 size_t fst_backward_workspace_size(const FstProblem* prob) {
@@ -90,8 +97,17 @@ int fst_forward(const FstForwardArgs* a, void* stream) {
       return fail(FST_ERR_INVALID, "forward: q, k, v, out and lse are required");
     if (p.use_attn_bias && !a->u) return fail(FST_ERR_INVALID, "forward: u required (attn bias)");
   }
+  const size_t need = fst_forward_workspace_size(&p);
+  if (need > 0 && (!a->workspace || a->workspace_bytes < need))
+    return fail(FST_ERR_WORKSPACE, "forward: workspace %zu bytes < required %zu",
+                a->workspace_bytes, need);
   cudaGetLastError();  // clear a stale error so the check below is ours
-  rc = fst::simt::launch_fwd(*a, (cudaStream_t)stream);
+  if (fst::tc::fwd_supported(p)) {
+    cudaMemsetAsync(a->workspace, 0, 4, (cudaStream_t)stream);  // device status word
+    rc = fst::tc::launch_fwd(*a, (cudaStream_t)stream);
+  } else {
+    rc = fst::simt::launch_fwd(*a, (cudaStream_t)stream);
+  }
   if (rc) return fail(rc, "forward launch failed");
   return cuda_status("forward launch");
 }
@@ -118,6 +134,8 @@ int fst_backward(const FstBackwardArgs* a, void* stream) {
   if (rc) return fail(rc, "backward launch failed");
   return cuda_status("backward launch");
 }
+
+int64_t fst_kernel_launches(void) { return fst::g_launches.load(std::memory_order_relaxed); }
 
 int fst_last_error(char* buf, size_t len) {
   const int n = (int)strlen(g_err);

@@ -393,6 +393,7 @@ static int launch_fwd_t(const FstForwardArgs& a, cudaStream_t st) {
   const int64_t n = a.prob.total_rows * a.prob.heads;
   if (n == 0) return FST_OK;
   fwd_kernel<T><<<(unsigned)((n + 127) / 128), 128, 0, st>>>(a);
+  count_launch();
   return FST_OK;
 }
 
@@ -406,9 +407,11 @@ static int launch_bwd_t(const FstBackwardArgs& a, cudaStream_t st) {
     const unsigned grid = (unsigned)((n + 127) / 128);
     bwd_rows_kernel<T><<<grid, 128, 0, st>>>(a, hbuf, gbuf);
     bwd_cols_kernel<T><<<grid, 128, 0, st>>>(a);
+    count_launch(2);
   }
   const int64_t chunk = (n + kDwParts - 1) / kDwParts;
   dw_partial_kernel<T><<<kDwParts, 256, 0, st>>>(a, hbuf, gbuf, chunk > 0 ? chunk : 1);
+  count_launch();
   return FST_OK;
 }
 

@@ -1,0 +1,210 @@
+// Device building blocks of the tensor-core kernels (sm_100a):
+// warp-level bf16/fp16 MMA, ldmatrix/movmatrix, cp.async with mbarrier
+// completion, named barriers, bounded mbarrier waits and the sin/cos of the
+// pair embedding.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+#include "fst_common.cuh"
+
+namespace fst {
+namespace tc {
+
+// ---- element types ---------------------------------------------------------
+
+template <typename T> struct Elem;
+template <> struct Elem<__nv_bfloat16> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  static __device__ __forceinline__ float lo(uint32_t v) { return __uint_as_float(v << 16); }
+  static __device__ __forceinline__ float hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
+};
+template <> struct Elem<__half> {
+  static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+    uint32_t r;
+    asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+    return r;
+  }
+  static __device__ __forceinline__ float lo(uint32_t v) {
+    return __half2float(__ushort_as_half((unsigned short)(v & 0xffff)));
+  }
+  static __device__ __forceinline__ float hi(uint32_t v) {
+    return __half2float(__ushort_as_half((unsigned short)(v >> 16)));
+  }
+};
+
+// D += A(16x16) * B(16x8), fp32 accumulate. A/B are both bf16 or both fp16.
+template <typename T>
+__device__ __forceinline__ void mma16816(float* d, const uint32_t* a, const uint32_t* b);
+template <>
+__device__ __forceinline__ void mma16816<__nv_bfloat16>(float* d, const uint32_t* a,
+                                                        const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+template <>
+__device__ __forceinline__ void mma16816<__half>(float* d, const uint32_t* a, const uint32_t* b) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b[0]), "r"(b[1]));
+}
+
+// ---- shared memory access --------------------------------------------------
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t* r) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];\n"
+               : "=r"(r[0]), "=r"(r[1])
+               : "r"(addr));
+}
+
+// In-register transpose of an 8x8 b16 tile held in mma fragment order.
+__device__ __forceinline__ uint32_t movm_t(uint32_t x) {
+  uint32_t r;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;\n" : "=r"(r) : "r"(x));
+  return r;
+}
+
+__device__ __forceinline__ void sts_v2(uint32_t addr, float a, float b) {
+  asm volatile("st.shared.v2.f32 [%0], {%1, %2};\n" ::"r"(addr), "f"(a), "f"(b) : "memory");
+}
+__device__ __forceinline__ void sts_u32(uint32_t addr, uint32_t v) {
+  asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(addr), "r"(v) : "memory");
+}
+__device__ __forceinline__ float2 lds_v2(uint32_t addr) {
+  float2 r;
+  asm volatile("ld.shared.v2.f32 {%0, %1}, [%2];\n" : "=f"(r.x), "=f"(r.y) : "r"(addr) : "memory");
+  return r;
+}
+
+// Row swizzle of a tile whose rows are `RB` bytes (a power of two, 32..128):
+// the 16-byte chunk c of row r moves to chunk c ^ ((r / (128/RB)) % (RB/16)),
+// so 8 consecutive rows read at the same logical chunk hit 8 distinct
+// 16-byte bank groups (conflict-free ldmatrix).
+template <int RB>
+__device__ __forceinline__ uint32_t swz(int row, int chunk) {
+  static_assert(RB == 32 || RB == 64 || RB == 128, "row bytes");
+  constexpr int kChunks = RB / 16;
+  constexpr int kRowsPerLine = 128 / RB;
+  return (uint32_t)(row * RB + ((chunk ^ ((row / kRowsPerLine) % kChunks)) << 4));
+}
+
+// ---- async copies and barriers --------------------------------------------
+
+__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(dst), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() {
+  asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+// Wait until at most N of this thread's committed cp.async groups are pending.
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+// Arrive on `bar` once all of this thread's prior cp.async copies completed.
+__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
+  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }\n" ::"r"(bar)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Error bits a kernel ORs into the caller's status word.
+constexpr int kErrTimeout = 1;
+
+// Spin on an mbarrier phase with an iteration cap (each try_wait already
+// suspends for a hardware-chosen interval). On timeout the status word gets
+// kErrTimeout and the caller carries on with whatever is in shared memory:
+// the kernel always terminates and the host reports the error.
+constexpr long kSpinLimit = 1L << 26;
+__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, int* status) {
+  long it = 0;
+  while (!mbar_try_wait(bar, parity)) {
+    if (++it > kSpinLimit) {
+      if (status) atomicOr(status, kErrTimeout);
+      return;
+    }
+  }
+}
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- math ------------------------------------------------------------------
+
+__device__ __forceinline__ float ex2(float x) {
+  float r;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+
+// sin and cos of x*f with Cody-Waite argument reduction (W. J. Cody and
+// W. Waite, "Software Manual for the Elementary Functions", 1980): 2*pi is
+// split into C1 + C2 + C3 where C1 carries 8 significant bits, so n*C1 is
+// exact for |n| < 2^16 and x*f - n*C1 is formed by one FMA from the exact
+// product. The reduced argument r in [-pi, pi] goes to the hardware
+// sin.approx / cos.approx, whose absolute error is ~1e-6 on that interval.
+// |x*f| <= 4096 here (x is clipped), so |n| <= 652.
+__device__ __forceinline__ void sincos_xf(float x, float f, float& s, float& c) {
+  const float kInv2Pi = 0.15915494309189535f;
+  const float kC1 = 6.28125f;                 // 2*pi rounded to 12 bits
+  const float kC2 = 1.9353071795864769e-03f;  // next 24 bits of 2*pi
+  const float kC3 = 1.0253377e-11f;           // 2*pi - C1 - C2
+  const float n = rintf(x * f * kInv2Pi);
+  float r = fmaf(x, f, -n * kC1);
+  r = fmaf(-n, kC2, r);
+  r = fmaf(-n, kC3, r);
+  s = __sinf(r);
+  c = __cosf(r);
+}
+
+}  // namespace tc
+}  // namespace fst

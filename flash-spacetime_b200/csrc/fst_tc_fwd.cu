@@ -1,0 +1,795 @@
+// Tensor-core forward kernel (bf16 / fp16 inputs) of fused spacetime-bias
+// attention for sm_100a.
+//
+// What it computes is upstream's flash_spacetime_fwd_kernel
+// (src/flash_spacetime/forward.py:63-219) plus the host epilogue of
+// flash_spacetime_forward (forward.py:333-345):
+//   s_ij = qt_i . k_j + u_i . E_ij           (u = (q*scale) W, from the host)
+//   P    = online softmax over the event's keys
+//   out  = sum_j P v_j / l + (sum_j P E_ij / l) W^T + b,  lse = log sum_j exp s
+//
+// How it is laid out on B200 (one CTA = one event x BM queries x <= 12 heads):
+//
+//   head warps  (one per head): own BM query rows of their head. They run
+//               QK^T and PV on the tensor cores (m16n8k16, fp32 accumulate,
+//               O in registers), add the pair bias, and do the online
+//               softmax with exp2 on the MUFU pipe.
+//   E warps     (BM / QPE of them): own QPE query rows each, all heads. They
+//               evaluate the C-channel embedding E_ij of every pair once (not
+//               once per head) directly in mma B-fragment order, form the
+//               logit bias u_q . E_qj for all heads with one MMA per query
+//               (heads on M), and accumulate A'_q = sum_j P_qj E_qj per query
+//               (heads on M, keys on K) from the head warps' P.
+//
+// Each head warp streams its own head's K and V 16-key chunks into a
+// 2-stage shared-memory ring with cp.async (prefetch distance one chunk);
+// each E warp streams its own copy of the key coordinates the same way. No
+// operand stage is shared between warps, so no cross-warp barrier guards
+// the ring.
+//
+// The two consumer groups exchange, per chunk, the fp32 bias tile (E warps
+// -> head warps) and the bf16/fp16 P tile plus the online-softmax rescale
+// factors (head warps -> E warps) through double-buffered shared memory,
+// handed over with named barriers (full/empty pairs). The embedding is never
+// written to memory and nothing of size O(L^2) exists anywhere.
+//
+// There are no spin waits: cp.async completion is awaited per thread and
+// every named barrier is reached by all head and E warps in the same order.
+
+#include <cuda_runtime.h>
+
+#include "fst_internal.h"
+#include "fst_tc_common.cuh"
+
+namespace fst {
+namespace tc {
+
+constexpr int kHeadsPerCta = 12;
+
+template <int DH, int C>
+struct FwdShape {
+  static constexpr int BM = (DH <= 32 && C <= 32) ? 32 : 16;  // query rows per CTA
+  static constexpr int RG = BM / 16;                          // 16-row groups
+  static constexpr int BN = 16;                               // keys per chunk
+  static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1); // queries per E warp
+  static constexpr int NE = BM / QPE;                         // E warps
+  static constexpr int HP = kHeadsPerCta;
+  static constexpr int NWARPS = HP + NE;                      // max warps per CTA
+  static constexpr int KSD = DH / 16, NTD = DH / 8;
+  static constexpr int KSC = C / 16, NTC = C / 8;
+  static constexpr int F = C / 2;                             // frequencies
+  static constexpr int FG = F / 8;                            // frequency groups per lane
+  static constexpr int DHP = DH <= 16 ? 16 : (DH <= 32 ? 32 : 64);
+  static constexpr int CP = C <= 16 ? 16 : (C <= 32 ? 32 : 64);
+  static constexpr int RBD = DHP * 2;                         // bytes per Q/K/V smem row
+  static constexpr int RBC = CP * 2;                          // bytes per u / W smem row
+  // fp32 bias tile: row (q, h) holds 16 keys + 8 pad floats; q stride padded
+  // to 8 (mod 32) words so both the E-warp stores and head-warp loads are
+  // free of bank conflicts.
+  static constexpr int BROW = 24;
+  static constexpr int BQ = ((HP * BROW + 31) / 32) * 32 + 8;
+  // P tile: per query 16 head rows x 8 words (16 keys) + 4 pad words.
+  static constexpr int PQ = 16 * 8 + 4;
+
+  // Shared memory carve-up (bytes). The Q and u staging tiles are read into
+  // registers once, before the key loop; the bias / P / alpha exchange tiles
+  // of the loop then reuse the same bytes.
+  static constexpr int SZ_Q = HP * BM * RBD;
+  static constexpr int SZ_U = BM * 16 * RBC;
+  static constexpr int SZ_B = BM * BQ * 4;                    // one bias stage
+  static constexpr int SZ_R = BM * HP * DH * 4;               // epilogue R reuses bias
+  static constexpr int SZ_BR = (2 * SZ_B > SZ_R) ? 2 * SZ_B : SZ_R;
+  static constexpr int SZ_P = BM * PQ * 4;                    // one P stage
+  static constexpr int SZ_A = 2 * BM * HP * 4;                // alpha, both stages
+  static constexpr int SZ_STAGE = SZ_Q + SZ_U;
+  static constexpr int SZ_LOOP = SZ_BR + 2 * SZ_P + SZ_A;
+  static constexpr int SZ_UNION = SZ_STAGE > SZ_LOOP ? SZ_STAGE : SZ_LOOP;
+  static constexpr int OFF_Q = 0;
+  static constexpr int OFF_U = OFF_Q + SZ_Q;
+  static constexpr int OFF_B = 0;                             // bias [2][BM][BQ] fp32
+  static constexpr int OFF_P = OFF_B + SZ_BR;                 // P [2][BM][PQ] words
+  static constexpr int OFF_A = OFF_P + 2 * SZ_P;              // alpha [2][BM][HP]
+  static constexpr int OFF_W = SZ_UNION;                      // W hi, W lo: [DH][CP]
+  static constexpr int SZ_W = 2 * DH * RBC;
+  static constexpr int OFF_K = OFF_W + SZ_W;
+  static constexpr int SZ_KV = HP * BN * RBD;                 // one stage of K (or V)
+  static constexpr int OFF_V = OFF_K + 2 * SZ_KV;
+  static constexpr int OFF_C = OFF_V + 2 * SZ_KV;             // key coords [NE][2][BN][4]
+  static constexpr int OFF_QC = OFF_C + NE * 2 * BN * 16;     // query coords [BM][4]
+  static constexpr int OFF_L = OFF_QC + BM * 16;              // row sums [BM][HP]
+  static constexpr int SMEM = OFF_L + BM * HP * 4;
+  static_assert(SMEM <= 227 * 1024, "shared memory budget");
+};
+
+// Named barrier ids (0 is __syncthreads).
+__device__ __forceinline__ int bar_bias_full(int s) { return 1 + s; }
+__device__ __forceinline__ int bar_bias_empty(int s) { return 3 + s; }
+__device__ __forceinline__ int bar_p_full(int s) { return 5 + s; }
+__device__ __forceinline__ int bar_p_empty(int s) { return 7 + s; }
+
+// Event and query block of this CTA. Padded layout: grid (L/BM, B, groups).
+// Packed layout: blockIdx.x indexes the flattened list of (event, block)
+// tiles whose exclusive prefix is tile_start[0..B].
+__device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_start, int& b,
+                                         int& qb) {
+  if (!p.packed) {
+    b = blockIdx.y;
+    qb = blockIdx.x;
+    return true;
+  }
+  const int t = blockIdx.x;
+  if (t >= tile_start[p.batch]) return false;
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {  // last b with tile_start[b] <= t
+    int mid = (lo + hi + 1) >> 1;
+    if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  b = lo;
+  qb = t - tile_start[b];
+  return true;
+}
+
+template <typename T, int DH, int C>
+__global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
+    fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group,
+                  int* status) {
+  using S = FwdShape<DH, C>;
+  using E = Elem<T>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const FstProblem& p = a.prob;
+
+  int b, qb;
+  if (!fwd_tile(p, tile_start, b, qb)) return;
+  const EventSpan ev = event_span(p, b);
+  const int q0 = qb * S::BM;
+  // Heads are split into gridDim.z groups of heads_per_group (<= HP); the
+  // block is sized for heads_per_group head warps, so in a shorter last group
+  // the surplus warps idle (they only join the CTA-wide barriers).
+  const int h0 = blockIdx.z * heads_per_group;
+  const int NH = min(heads_per_group, p.heads - h0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NE = S::NE;
+  const int nthreads = blockDim.x;
+  const T* __restrict__ gq = (const T*)a.q;
+  const T* __restrict__ gk = (const T*)a.k;
+  const T* __restrict__ gv = (const T*)a.v;
+  const T* __restrict__ gu = (const T*)a.u;
+  T* __restrict__ gout = (T*)a.out;
+  const bool attn = p.use_attn_bias != 0;
+  const bool act = p.use_act_bias != 0;
+
+  // A query block entirely past the event's end: padding rows (padded
+  // layout) get zeros; nothing else to do.
+  if (q0 >= ev.len) {
+    if (!p.packed) {
+      for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
+        const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
+        if (q >= p.max_len) continue;
+        const int64_t row = ev.row0 + q;
+        T* o = gout + vec_off(p, row, h, DH);
+        for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
+        a.lse[stat_off(p, row, h)] = 0.f;
+      }
+    }
+    return;
+  }
+  const int nvalid_q = min(S::BM, ev.len - q0);
+  const int nchunks = (ev.len + S::BN - 1) / S::BN;
+  const int NBAR = (NH + NE) * 32;  // threads in the head/E-warp hand-offs
+
+  const uint32_t sm = smem_u32(smem);
+  const uint32_t sQ = sm + S::OFF_Q, sU = sm + S::OFF_U, sW = sm + S::OFF_W;
+  const uint32_t sK = sm + S::OFF_K, sV = sm + S::OFF_V, sC = sm + S::OFF_C;
+  const uint32_t sB = sm + S::OFF_B, sP = sm + S::OFF_P, sA = sm + S::OFF_A;
+  const uint32_t sL = sm + S::OFF_L;
+  float* fQC = (float*)(smem + S::OFF_QC);
+
+  // ---------------- prologue: stage Q (scaled), u, W, query coords --------
+  {
+    constexpr int QCH = DH / 8;  // 16-byte chunks per q row
+    for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
+      const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (q < nvalid_q) {
+        const uint4 raw = *(const uint4*)(gq + vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8);
+        const uint32_t* w = (const uint32_t*)&raw;
+        uint32_t* o = (uint32_t*)&v;
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[i] = E::pack(E::lo(w[i]) * p.scale, E::hi(w[i]) * p.scale);
+      }
+      *(uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c)) = v;
+    }
+    constexpr int UCH = S::CP / 8;
+    for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
+      const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (attn && q < nvalid_q && h < NH && c * 8 < C)
+        v = *(const uint4*)(gu + vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8);
+      *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = v;
+    }
+    // W^T operand of the epilogue, split into hi + lo halves of the 16-bit type
+    // so that (A'/l) W^T keeps W at ~fp32 accuracy.
+    for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
+      const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
+      float w0 = 0.f, w1 = 0.f;
+      if (act && 2 * c2 < C) {
+        w0 = p.weight[(int64_t)d * C + 2 * c2];
+        w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
+      }
+      const uint32_t hi = E::pack(w0, w1);
+      const uint32_t lo = E::pack(w0 - E::lo(hi), w1 - E::hi(hi));
+      const uint32_t off = swz<S::RBC>(d, c2 / 4) + (c2 % 4) * 4;
+      *(uint32_t*)(smem + S::OFF_W + off) = hi;
+      *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
+    }
+    for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
+      const int q = idx / 4, k = idx % 4;
+      fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
+    }
+  }
+  __syncthreads();
+
+  const int m4 = lane & 3, r8 = lane >> 2;
+  // Operand fragments that stay in registers for the whole key loop.
+  uint32_t qa[S::RG][S::KSD][4];   // head warps: scaled Q (queries on M)
+  uint32_t ua[S::QPE][S::KSC][4];  // E warps: u_q (heads on M)
+  const bool idle = warp >= NH + NE;
+  if (warp < NH) {
+#pragma unroll
+    for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+      for (int ks = 0; ks < S::KSD; ++ks) {
+        const int mi = lane >> 3;
+        const int q = rg * 16 + (mi & 1) * 8 + (lane & 7);
+        ldsm_x4(sQ + warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1)), qa[rg][ks]);
+      }
+  } else if (!idle) {
+    const int qe = (warp - NH) * S::QPE;
+#pragma unroll
+    for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+      for (int ks = 0; ks < S::KSC; ++ks) {
+        const int mi = lane >> 3;
+        const int h = (mi & 1) * 8 + (lane & 7);
+        ldsm_x4(sU + swz<S::RBC>((qe + t) * 16 + h, 2 * ks + (mi >> 1)), ua[t][ks]);
+      }
+  }
+  __syncthreads();  // the staging tiles are dead; the exchange tiles take their place
+  for (int idx = threadIdx.x; idx < 2 * S::SZ_P / 4; idx += nthreads)
+    ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+  __syncthreads();
+
+  if (idle) {
+    __syncthreads();
+    __syncthreads();
+    return;
+  }
+  if (warp >= NH) {
+    // ======================= E warps ======================================
+    const int e = warp - NH;
+    const int qe = e * S::QPE;  // first query row owned by this warp
+    // This lane evaluates frequencies 8g + 2*m4 + r (g < FG, r < 2).
+    float fr[S::FG][2];
+#pragma unroll
+    for (int g = 0; g < S::FG; ++g) {
+      fr[g][0] = p.freqs[8 * g + 2 * m4];
+      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+    }
+    // Coordinates of the query this lane evaluates x for (lane group m4).
+    const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
+    Coord4 cq;
+    cq.x = fQC[qx_row * 4 + 0];
+    cq.y = fQC[qx_row * 4 + 1];
+    cq.z = fQC[qx_row * 4 + 2];
+    cq.t = fQC[qx_row * 4 + 3];
+
+    // Private ring of key coordinates: [2 stages][BN][4] fp32.
+    const uint32_t c_ring = sC + e * 2 * S::BN * 16;
+    auto load_coords = [&](int n) {
+      if (n < nchunks && lane < S::BN) {
+        const int j = n * S::BN + lane;
+        const uint32_t dst = c_ring + ((n & 1) * S::BN + lane) * 16;
+        if (j < ev.len)
+          cp_async16(dst, p.feats + (ev.row0 + j) * p.feat_stride);
+        else
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
+      }
+      cp_async_commit();
+    };
+    load_coords(0);
+    load_coords(1);
+
+    float acc[S::QPE][S::NTC][4];
+#pragma unroll
+    for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+      for (int nc = 0; nc < S::NTC; ++nc)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[t][nc][i] = 0.f;
+
+    for (int n = 0; n < nchunks; ++n) {
+      const int s = n & 1;
+      cp_async_wait<1>();
+      __syncwarp();
+      // x for (query qx_row, key nt*8 + r8).
+      float xl[2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const float4 ck = *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + nt * 8 + r8) * 16);
+        Coord4 c4;
+        c4.x = ck.x;
+        c4.y = ck.y;
+        c4.z = ck.z;
+        c4.t = ck.w;
+        xl[nt] = pair_angle(cq, c4);
+      }
+      __syncwarp();
+      load_coords(n + 2);  // stage s is free again
+      if (!(attn || act)) continue;
+
+      uint32_t eb[S::QPE][2][S::KSC][2];  // E B-fragments: (k = channel, n = key)
+      if (attn && n >= 2) named_sync(bar_bias_empty(s), NBAR);
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t) {
+        float sn[2][S::FG][2], cs[2][S::FG][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+#pragma unroll
+          for (int g = 0; g < S::FG; ++g)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+        }
+        // Channel c < F is sin(x f_c); c >= F is cos(x f_{c-F}). The lane's
+        // fragment slots are channels 16 ks + 8 hi + 2 m4 + r.
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks)
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+              const int cb = 16 * ks + 8 * hi;
+              const int g = (cb % S::F) / 8;
+              const bool is_sin = cb < S::F;
+              const float v0 = is_sin ? sn[nt][g][0] : cs[nt][g][0];
+              const float v1 = is_sin ? sn[nt][g][1] : cs[nt][g][1];
+              eb[t][nt][ks][hi] = E::pack(v0, v1);
+            }
+        if (attn) {
+          const int q = qe + t;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int ks = 0; ks < S::KSC; ++ks) mma16816<T>(d, ua[t][ks], eb[t][nt][ks]);
+            const uint32_t base = sB + s * S::SZ_B + (q * S::BQ + nt * 8 + 2 * m4) * 4;
+            if (r8 < NH) sts_v2(base + r8 * S::BROW * 4, d[0], d[1]);
+            if (r8 + 8 < NH) sts_v2(base + (r8 + 8) * S::BROW * 4, d[2], d[3]);
+          }
+        }
+      }
+      if (attn) named_arrive(bar_bias_full(s), NBAR);
+      if (act) {
+        named_sync(bar_p_full(s), NBAR);
+#pragma unroll
+        for (int t = 0; t < S::QPE; ++t) {
+          const int q = qe + t;
+          const float* alph = (const float*)(smem + S::OFF_A + (s * S::BM + q) * S::HP * 4);
+          const float a0 = r8 < NH ? alph[r8] : 1.f;
+          const float a1 = r8 + 8 < NH ? alph[r8 + 8] : 1.f;
+          uint32_t pa[4];
+          {
+            const int mi = lane >> 3;
+            const int h = (mi & 1) * 8 + (lane & 7);
+            ldsm_x4(sP + s * S::SZ_P + (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4, pa);
+          }
+#pragma unroll
+          for (int nc = 0; nc < S::NTC; ++nc) {
+            acc[t][nc][0] *= a0;
+            acc[t][nc][1] *= a0;
+            acc[t][nc][2] *= a1;
+            acc[t][nc][3] *= a1;
+            // E^T B-fragment (k = key, n = channel) by transposing the 8x8
+            // blocks of the (k = channel, n = key) fragment in registers.
+            uint32_t bt[2];
+            bt[0] = movm_t(eb[t][0][nc >> 1][nc & 1]);
+            bt[1] = movm_t(eb[t][1][nc >> 1][nc & 1]);
+            mma16816<T>(acc[t][nc], pa, bt);
+          }
+        }
+        if (n + 2 < nchunks) named_arrive(bar_p_empty(s), NBAR);
+      }
+    }
+
+    __syncthreads();  // head warps published their row sums
+    if (act) {
+      // R_q = (A'_q / l) W^T  (heads on M, channels on K, head dim on N),
+      // with W split into hi + lo halves. Stored fp32 as [q][h][d].
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t) {
+        const int q = qe + t;
+        const float* lsum = (const float*)(smem + S::OFF_L + q * S::HP * 4);
+        const float il0 = r8 < NH ? 1.f / lsum[r8] : 0.f;
+        const float il1 = r8 + 8 < NH ? 1.f / lsum[r8 + 8] : 0.f;
+        uint32_t aa[S::KSC][4];
+#pragma unroll
+        for (int ks = 0; ks < S::KSC; ++ks) {
+          aa[ks][0] = E::pack(acc[t][2 * ks][0] * il0, acc[t][2 * ks][1] * il0);
+          aa[ks][1] = E::pack(acc[t][2 * ks][2] * il1, acc[t][2 * ks][3] * il1);
+          aa[ks][2] = E::pack(acc[t][2 * ks + 1][0] * il0, acc[t][2 * ks + 1][1] * il0);
+          aa[ks][3] = E::pack(acc[t][2 * ks + 1][2] * il1, acc[t][2 * ks + 1][3] * il1);
+        }
+#pragma unroll
+        for (int nd = 0; nd < S::NTD; ++nd) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks) {
+#pragma unroll
+            for (int part = 0; part < 2; ++part) {
+              // B (k = channel, n = d) = W[d][c]: rows d, 8 channels per row.
+              uint32_t wb[2];
+              const int mi = (lane >> 3) & 1;
+              ldsm_x2(sW + part * DH * S::RBC + swz<S::RBC>(nd * 8 + (lane & 7), 2 * ks + mi), wb);
+              mma16816<T>(d, aa[ks], wb);
+            }
+          }
+          float* rs = (float*)(smem + S::OFF_B);
+          if (r8 < NH) {
+            rs[(q * S::HP + r8) * DH + nd * 8 + 2 * m4] = d[0];
+            rs[(q * S::HP + r8) * DH + nd * 8 + 2 * m4 + 1] = d[1];
+          }
+          if (r8 + 8 < NH) {
+            rs[(q * S::HP + r8 + 8) * DH + nd * 8 + 2 * m4] = d[2];
+            rs[(q * S::HP + r8 + 8) * DH + nd * 8 + 2 * m4 + 1] = d[3];
+          }
+        }
+      }
+    }
+    __syncthreads();  // R published
+    return;
+  } else {
+    // ======================= head warps ===================================
+    const int hl = warp;  // local head
+    const int h = h0 + hl;
+    // Private ring of this head's K and V chunks: [2 stages][BN][DHP].
+    auto load_kv = [&](int n) {
+      if (n < nchunks) {
+        constexpr int CH = DH / 8;
+        const int j0 = n * S::BN;
+        const uint32_t k_st = sK + (n & 1) * S::SZ_KV + hl * S::BN * S::RBD;
+        const uint32_t v_st = sV + (n & 1) * S::SZ_KV + hl * S::BN * S::RBD;
+        for (int idx = lane; idx < S::BN * CH; idx += 32) {
+          const int c = idx % CH, j = idx / CH;
+          const uint32_t off = swz<S::RBD>(j, c);
+          if (j0 + j < ev.len) {
+            const int64_t go = vec_off(p, ev.row0 + j0 + j, h, DH) + c * 8;
+            cp_async16(k_st + off, gk + go);
+            cp_async16(v_st + off, gv + go);
+          } else {
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(k_st + off), "r"(0));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(v_st + off), "r"(0));
+          }
+        }
+      }
+      cp_async_commit();
+    };
+    load_kv(0);
+    load_kv(1);
+
+    float o[S::RG][S::NTD][4];
+    float mrun[S::RG][2], lrun[S::RG][2];
+#pragma unroll
+    for (int rg = 0; rg < S::RG; ++rg) {
+#pragma unroll
+      for (int nd = 0; nd < S::NTD; ++nd)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[rg][nd][i] = 0.f;
+      mrun[rg][0] = mrun[rg][1] = -INFINITY;
+      lrun[rg][0] = lrun[rg][1] = 0.f;
+    }
+
+    for (int n = 0; n < nchunks; ++n) {
+      const int s = n & 1;
+      const int j0 = n * S::BN;
+      cp_async_wait<1>();
+      __syncwarp();
+      const uint32_t k_st = sK + s * S::SZ_KV + hl * S::BN * S::RBD;
+      const uint32_t v_st = sV + s * S::SZ_KV + hl * S::BN * S::RBD;
+
+      // K B-fragments (k = head dim, n = key): kb[nt][ks][2].
+      uint32_t kb[2][S::KSD][2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int kp = 0; kp < (S::KSD + 1) / 2; ++kp) {
+          const int mi = lane >> 3;
+          const int chunk = 4 * kp + mi;  // d chunk (8 elements)
+          uint32_t r[4];
+          if (S::KSD - 2 * kp >= 2) {
+            ldsm_x4(k_st + swz<S::RBD>(nt * 8 + (lane & 7), chunk), r);
+            kb[nt][2 * kp][0] = r[0];
+            kb[nt][2 * kp][1] = r[1];
+            kb[nt][2 * kp + 1][0] = r[2];
+            kb[nt][2 * kp + 1][1] = r[3];
+          } else {
+            ldsm_x2(k_st + swz<S::RBD>(nt * 8 + (lane & 7), 4 * kp + (mi & 1)), r);
+            kb[nt][2 * kp][0] = r[0];
+            kb[nt][2 * kp][1] = r[1];
+          }
+        }
+
+      float sc[S::RG][2][4];
+#pragma unroll
+      for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+          for (int i = 0; i < 4; ++i) sc[rg][nt][i] = 0.f;
+#pragma unroll
+          for (int ks = 0; ks < S::KSD; ++ks) mma16816<T>(sc[rg][nt], qa[rg][ks], kb[nt][ks]);
+        }
+
+      if (attn) {
+        named_sync(bar_bias_full(s), NBAR);
+#pragma unroll
+        for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            const int q = rg * 16 + r8;
+            const uint32_t base = sB + s * S::SZ_B + (hl * S::BROW + nt * 8 + 2 * m4) * 4;
+            const float2 b0 = lds_v2(base + q * S::BQ * 4);
+            const float2 b1 = lds_v2(base + (q + 8) * S::BQ * 4);
+            sc[rg][nt][0] += b0.x;
+            sc[rg][nt][1] += b0.y;
+            sc[rg][nt][2] += b1.x;
+            sc[rg][nt][3] += b1.y;
+          }
+        if (n + 2 < nchunks) named_arrive(bar_bias_empty(s), NBAR);
+      }
+
+      // Online softmax in the log2 domain (upstream forward.py:170-185).
+      const bool tail = j0 + S::BN > ev.len;
+      uint32_t pa[S::RG][4];
+      float alpha[S::RG][2];
+#pragma unroll
+      for (int rg = 0; rg < S::RG; ++rg) {
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i) {
+            float v = sc[rg][nt][i] * kLog2e;
+            if (tail && j0 + nt * 8 + 2 * m4 + (i & 1) >= ev.len) v = -INFINITY;
+            sc[rg][nt][i] = v;
+          }
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+          float mx = fmaxf(fmaxf(sc[rg][0][2 * rh], sc[rg][0][2 * rh + 1]),
+                           fmaxf(sc[rg][1][2 * rh], sc[rg][1][2 * rh + 1]));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+          mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+          const float mnew = fmaxf(mrun[rg][rh], mx);
+          const float muse = mnew == -INFINITY ? 0.f : mnew;
+          const float al = ex2(mrun[rg][rh] - muse);
+          float ps = 0.f;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int c = 0; c < 2; ++c) {
+              const float pv = ex2(sc[rg][nt][2 * rh + c] - muse);
+              sc[rg][nt][2 * rh + c] = pv;
+              ps += pv;
+            }
+          lrun[rg][rh] = lrun[rg][rh] * al + ps;
+          mrun[rg][rh] = mnew;
+          alpha[rg][rh] = al;
+#pragma unroll
+          for (int nd = 0; nd < S::NTD; ++nd) {
+            o[rg][nd][2 * rh] *= al;
+            o[rg][nd][2 * rh + 1] *= al;
+          }
+        }
+        pa[rg][0] = E::pack(sc[rg][0][0], sc[rg][0][1]);
+        pa[rg][1] = E::pack(sc[rg][0][2], sc[rg][0][3]);
+        pa[rg][2] = E::pack(sc[rg][1][0], sc[rg][1][1]);
+        pa[rg][3] = E::pack(sc[rg][1][2], sc[rg][1][3]);
+      }
+
+      if (act) {
+        if (n >= 2) named_sync(bar_p_empty(s), NBAR);
+        const uint32_t pbase = sP + s * S::SZ_P + (hl * 8 + m4) * 4;
+#pragma unroll
+        for (int rg = 0; rg < S::RG; ++rg) {
+          const int q = rg * 16 + r8;
+          sts_u32(pbase + q * S::PQ * 4, pa[rg][0]);
+          sts_u32(pbase + q * S::PQ * 4 + 16, pa[rg][2]);
+          sts_u32(pbase + (q + 8) * S::PQ * 4, pa[rg][1]);
+          sts_u32(pbase + (q + 8) * S::PQ * 4 + 16, pa[rg][3]);
+          if (m4 == 0) {
+            float* al = (float*)(smem + S::OFF_A + s * S::BM * S::HP * 4);
+            al[q * S::HP + hl] = alpha[rg][0];
+            al[(q + 8) * S::HP + hl] = alpha[rg][1];
+          }
+        }
+        named_arrive(bar_p_full(s), NBAR);
+      }
+
+      // O += P V (V B-fragments: k = key, n = head dim, via ldmatrix.trans).
+#pragma unroll
+      for (int np = 0; np < (S::NTD + 1) / 2; ++np) {
+        const int mi = lane >> 3;
+        uint32_t r[4];
+        if (S::NTD - 2 * np >= 2) {
+          ldsm_x4_t(v_st + swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np + (mi >> 1)), r);
+#pragma unroll
+          for (int rg = 0; rg < S::RG; ++rg) {
+            mma16816<T>(o[rg][2 * np], pa[rg], r);
+            mma16816<T>(o[rg][2 * np + 1], pa[rg], r + 2);
+          }
+        } else {
+          ldsm_x2_t(v_st + swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np), r);
+#pragma unroll
+          for (int rg = 0; rg < S::RG; ++rg) mma16816<T>(o[rg][2 * np], pa[rg], r);
+        }
+      }
+      __syncwarp();
+      load_kv(n + 2);  // stage s is free again
+    }
+
+    // Row sums over the quad, published for the E warps' A' normalisation.
+#pragma unroll
+    for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        float l = lrun[rg][rh];
+        l += __shfl_xor_sync(0xffffffffu, l, 1);
+        l += __shfl_xor_sync(0xffffffffu, l, 2);
+        lrun[rg][rh] = l;
+        if (m4 == 0) ((float*)(smem + S::OFF_L))[(rg * 16 + r8 + 8 * rh) * S::HP + hl] = l;
+      }
+    __syncthreads();
+    __syncthreads();  // E warps published R = (A'/l) W^T
+
+    const float* rs = (const float*)(smem + S::OFF_B);
+#pragma unroll
+    for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        const int q = rg * 16 + r8 + 8 * rh;
+        const bool valid = q < nvalid_q;
+        if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
+        const int64_t row = ev.row0 + q0 + q;
+        const float il = valid ? 1.f / lrun[rg][rh] : 0.f;
+        T* orow = gout + vec_off(p, row, h, DH);
+#pragma unroll
+        for (int nd = 0; nd < S::NTD; ++nd) {
+          const int d = nd * 8 + 2 * m4;
+          float v0 = o[rg][nd][2 * rh] * il, v1 = o[rg][nd][2 * rh + 1] * il;
+          if (act && valid) {
+            v0 += rs[(q * S::HP + hl) * DH + d];
+            v1 += rs[(q * S::HP + hl) * DH + d + 1];
+            if (p.bias) {
+              v0 += p.bias[d];
+              v1 += p.bias[d + 1];
+            }
+          }
+          if (!valid) v0 = v1 = 0.f;
+          *(uint32_t*)(orow + d) = E::pack(v0, v1);
+        }
+        if (m4 == 0)
+          a.lse[stat_off(p, row, h)] =
+              valid ? (mrun[rg][rh] + __log2f(lrun[rg][rh])) * 0.6931471805599453f : 0.f;
+      }
+    return;
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+__global__ void tile_prefix_kernel(const int32_t* __restrict__ cu, int batch, int bm,
+                                   int* __restrict__ tile_start) {
+  // Single-CTA exclusive scan of ceil(len_b / bm) over the events.
+  __shared__ int warp_sums[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) carry = 0;
+  __syncthreads();
+  for (int base = 0; base < batch; base += blockDim.x) {
+    const int b = base + threadIdx.x;
+    const int v = b < batch ? (cu[b + 1] - cu[b] + bm - 1) / bm : 0;
+    int x = v;
+    const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, x, o);
+      if (lane >= o) x += y;
+    }
+    if (lane == 31) warp_sums[w] = x;
+    __syncthreads();
+    if (w == 0) {
+      int ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, ws, o);
+        if (lane >= o) ws += y;
+      }
+      warp_sums[lane] = ws;
+    }
+    __syncthreads();
+    const int incl = x + (w > 0 ? warp_sums[w - 1] : 0) + carry;
+    if (b < batch) tile_start[b] = incl - v;
+    __syncthreads();
+    if (threadIdx.x == blockDim.x - 1) carry = incl;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) tile_start[batch] = carry;
+}
+
+template <typename T, int DH, int C>
+static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_start,
+                            int* status) {
+  using S = FwdShape<DH, C>;
+  const FstProblem& p = a.prob;
+  static bool configured = false;  // per template instance
+  if (!configured) {
+    if (cudaFuncSetAttribute(fwd_tc_kernel<T, DH, C>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             S::SMEM) != cudaSuccess)
+      return FST_ERR_CUDA;
+    configured = true;
+  }
+  const int groups = (p.heads + S::HP - 1) / S::HP;
+  const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
+  const int threads = (per_group + S::NE) * 32;
+  dim3 grid;
+  if (p.packed) {
+    tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.batch, S::BM, tile_start);
+    count_launch();
+    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
+    grid = dim3((unsigned)upper, 1, groups);
+  } else {
+    grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
+  }
+  if (grid.x == 0 || grid.y == 0) return FST_OK;
+  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, status);
+  count_launch();
+  return FST_OK;
+}
+
+template <typename T>
+static int launch_fwd_t(const FstForwardArgs& a, cudaStream_t st, int* ts, int* status) {
+  const int D = a.prob.head_dim, C = a.prob.channels;
+#define FST_FWD_CASE(DD, CC) \
+  if (D == DD && C == CC) return launch_fwd_shape<T, DD, CC>(a, st, ts, status);
+  FST_FWD_CASE(32, 16)
+  FST_FWD_CASE(32, 32)
+  FST_FWD_CASE(32, 64)
+  FST_FWD_CASE(64, 32)
+  FST_FWD_CASE(64, 64)
+  FST_FWD_CASE(16, 16)
+  FST_FWD_CASE(48, 48)
+#undef FST_FWD_CASE
+  return FST_ERR_UNSUPPORTED;
+}
+
+bool fwd_supported(const FstProblem& p) {
+  if (p.dtype == FST_F32) return false;
+  const int D = p.head_dim, C = p.channels;
+  return (D == 32 && (C == 16 || C == 32 || C == 64)) || (D == 64 && (C == 32 || C == 64)) ||
+         (D == 16 && C == 16) || (D == 48 && C == 48);
+}
+
+size_t fwd_workspace(const FstProblem& p) {
+  return (size_t)(p.batch + 1) * sizeof(int) + 64;  // tile prefix + status
+}
+
+int launch_fwd(const FstForwardArgs& a, cudaStream_t st) {
+  int* ws = (int*)a.workspace;
+  int* status = ws;            // first 64 bytes: status word
+  int* tile_start = ws + 16;
+  if (a.prob.dtype == FST_BF16) return launch_fwd_t<__nv_bfloat16>(a, st, tile_start, status);
+  if (a.prob.dtype == FST_F16) return launch_fwd_t<__half>(a, st, tile_start, status);
+  return FST_ERR_UNSUPPORTED;
+}
+
+}  // namespace tc
+}  // namespace fst

@@ -37,6 +37,29 @@ _DTYPES = {
 }
 
 _freq_cache: Dict[Tuple[int, str], Tensor] = {}
+_kernel_timer: Optional[list] = None
+
+
+def set_kernel_timer(sink: Optional[list]) -> None:
+    """Record CUDA events around every library call into ``sink``.
+
+    Each entry is ``(entry point name, start event, end event)``, recorded on
+    the stream the kernels are launched on. Pass None to stop recording.
+    """
+    global _kernel_timer
+    _kernel_timer = sink
+
+
+def _timed_call(name: str, fn, args, device: torch.device) -> int:
+    if _kernel_timer is None:
+        return fn(*args)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record()
+    rc = fn(*args)
+    e1.record()
+    _kernel_timer.append((name, e0, e1))
+    return rc
 
 
 def _freqs(channels: int, device: torch.device) -> Tensor:
@@ -210,7 +233,9 @@ def fused_forward(pb: _Problem, q: Tensor, k: Tensor, v: Tensor) -> Tuple[Tensor
     a.q, a.k, a.v, a.u = _ptr(q), _ptr(k), _ptr(v), _ptr(u)
     a.out, a.lse = _ptr(out), _ptr(lse)
     a.workspace, a.workspace_bytes = _ptr(ws), nws
-    _lib.check(lib.fst_forward(ctypes.byref(a), _stream(pb.device)), "fst_forward")
+    rc = _timed_call("fst_forward", lib.fst_forward, (ctypes.byref(a), _stream(pb.device)),
+                     pb.device)
+    _lib.check(rc, "fst_forward")
     return out, lse
 
 
@@ -252,7 +277,9 @@ def fused_backward(
     a.dw_partial, a.delta, a.sigma = _ptr(dw_part), _ptr(delta), _ptr(sigma)
     a.ds_absmax = _ptr(absmax)
     a.workspace, a.workspace_bytes = _ptr(ws), nws
-    _lib.check(lib.fst_backward(ctypes.byref(a), _stream(pb.device)), "fst_backward")
+    rc = _timed_call("fst_backward", lib.fst_backward, (ctypes.byref(a), _stream(pb.device)),
+                     pb.device)
+    _lib.check(rc, "fst_backward")
 
     dw = db = None
     if pb.attn or pb.act:

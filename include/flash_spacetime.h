@@ -141,6 +141,10 @@ int fst_forward(const FstForwardArgs* args, void* stream);
 /* Fused backward (upstream backward.py:488-630). */
 int fst_backward(const FstBackwardArgs* args, void* stream);
 
+/* Number of CUDA kernels this library has launched in the process so far
+ * (benchmark bookkeeping; no counterpart upstream). */
+int64_t fst_kernel_launches(void);
+
 /* Copies the calling thread's last error message into buf (NUL-terminated).
  * Returns the message length. */
 int fst_last_error(char* buf, size_t len);

@@ -79,12 +79,14 @@ size_t fst_forward_workspace_size(const FstProblem* prob) {
 
 size_t fst_backward_workspace_size(const FstProblem* prob) {
   if (check_problem(prob) != FST_OK) return 0;
-  return fst::simt::bwd_workspace(*prob);
+  return fst::tc::bwd_supported(*prob) ? fst::tc::bwd_workspace(*prob)
+                                       : fst::simt::bwd_workspace(*prob);
 }
 
 int64_t fst_dw_partial_count(const FstProblem* prob) {
   if (check_problem(prob) != FST_OK) return 0;
-  return fst::simt::dw_parts(*prob);
+  return fst::tc::bwd_supported(*prob) ? fst::tc::rows_partials(*prob)
+                                       : fst::simt::dw_parts(*prob);
 }
 
 int fst_forward(const FstForwardArgs* a, void* stream) {
@@ -130,7 +132,10 @@ int fst_backward(const FstBackwardArgs* a, void* stream) {
     return fail(FST_ERR_WORKSPACE, "backward: workspace %zu bytes < required %zu",
                 a->workspace_bytes, need);
   cudaGetLastError();
-  rc = fst::simt::launch_bwd(*a, (cudaStream_t)stream);
+  if (fst::tc::bwd_supported(p))
+    rc = fst::tc::launch_bwd(*a, (cudaStream_t)stream);
+  else
+    rc = fst::simt::launch_bwd(*a, (cudaStream_t)stream);
   if (rc) return fail(rc, "backward launch failed");
   return cuda_status("backward launch");
 }

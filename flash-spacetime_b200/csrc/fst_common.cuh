@@ -104,4 +104,20 @@ __device__ __forceinline__ float pair_angle(const Coord4& a, const Coord4& b) {
   return kInputScale * fminf(fmaxf(d, -kClip), kClip);
 }
 
+// x * f - n * 2pi in [-pi, pi], with the product x*f taken exactly: Cody-Waite
+// argument reduction (W. J. Cody and W. Waite, "Software Manual for the
+// Elementary Functions", 1980) with 2*pi = C1 + C2 + C3, C1 = 6.28125 (8
+// significant bits, so n * C1 is exact for |n| < 2^16) and the first FMA
+// forming x*f - n*C1 from the unrounded product. |x*f| <= 4096 here.
+__device__ __forceinline__ float reduce_2pi(float x, float f) {
+  const float kInv2Pi = 0.15915494309189535f;
+  const float kC1 = 6.28125f;
+  const float kC2 = 1.9353071795864769e-03f;  // 2*pi - C1, rounded
+  const float kC3 = 1.0253377e-11f;           // 2*pi - C1 - C2
+  const float n = rintf(x * f * kInv2Pi);
+  float r = fmaf(x, f, -n * kC1);
+  r = fmaf(-n, kC2, r);
+  return fmaf(-n, kC3, r);
+}
+
 }  // namespace fst

@@ -56,7 +56,7 @@ __device__ __forceinline__ void embed(float x, const float* freqs, int C, float*
   for (int k = 0; k < kMax / 2; ++k) {
     if (k < half) {
       float sn, cs;
-      sincosf(x * freqs[k], &sn, &cs);
+      sincosf(reduce_2pi(x, freqs[k]), &sn, &cs);  // accurate sin/cos of the exact x*f
       e[k] = sn;
       e[k + half] = cs;
     }
@@ -236,7 +236,6 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
     for (int c = 0; c < C; ++c) hbuf[coff + c] = gbuf[coff + c] = 0.f;
     a.delta[so] = 0.f;
     a.sigma[so] = 0.f;
-    if (a.ds_absmax) a.ds_absmax[so] = 0.f;
     return;
   }
   const T* k = (const T*)a.k;
@@ -247,8 +246,15 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
 #pragma unroll
   for (int c = 0; c < kMax; ++c) e[c] = 0.f;
 
-  // Pass 1: D from the very P and dP that pass 2 turns into dS.
-  float spd = 0.f, sp = 0.f;
+  // One sweep over the keys, accumulating the dS contractions with D left
+  // symbolic (dS_ij = P_ij dP'_ij - D'_i P_ij): X = sum P dP' k, Y = sum P k,
+  // Hn = sum P dP' E, G = sum P E, a = sum P dP', ps = sum P. At the end
+  // D' = a / ps, so every sum of dS below is formed from the same P and dP'
+  // values and rowsum(dS) = a - D' ps vanishes up to one rounding.
+  float X[kMax], Y[kMax], Hn[kMax], G[kMax];
+#pragma unroll
+  for (int d = 0; d < kMax; ++d) X[d] = Y[d] = Hn[d] = G[d] = 0.f;
+  float acc_a = 0.f, acc_p = 0.f;
   for (int j = 0; j < t.ev.len; ++j) {
     const int64_t krow = t.ev.row0 + j;
     const int64_t koff = vec_off(p, krow, t.h, D);
@@ -256,38 +262,34 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
     load_vec<T>(v, koff, D, vv);
     float P, dP;
     p_dp<T>(a, r, krow, t.h, kv, vv, e, P, dP);
-    spd = fmaf(P, dP, spd);
-    sp += P;
-  }
-  const float Dr = sp > 0.f ? spd / sp : 0.f;
-
-  // Pass 2.
-  float dqp[kMax], H[kMax], G[kMax];
+    const float pd = P * dP;
+    acc_a += pd;
+    acc_p += P;
 #pragma unroll
-  for (int d = 0; d < kMax; ++d) dqp[d] = H[d] = G[d] = 0.f;
-  float sig = 0.f, amax = 0.f;
-  for (int j = 0; j < t.ev.len; ++j) {
-    const int64_t krow = t.ev.row0 + j;
-    const int64_t koff = vec_off(p, krow, t.h, D);
-    load_vec<T>(k, koff, D, kv);
-    load_vec<T>(v, koff, D, vv);
-    float P, dP;
-    p_dp<T>(a, r, krow, t.h, kv, vv, e, P, dP);
-    const float ds = P * (dP - Dr);
-    sig += ds;
-    amax = fmaxf(amax, fabsf(ds));
-#pragma unroll
-    for (int d = 0; d < kMax; ++d)
-      if (d < D) dqp[d] = fmaf(ds, kv[d], dqp[d]);
+    for (int d = 0; d < kMax; ++d) {
+      if (d < D) {
+        X[d] = fmaf(pd, kv[d], X[d]);
+        Y[d] = fmaf(P, kv[d], Y[d]);
+      }
+    }
 #pragma unroll
     for (int c = 0; c < kMax; ++c) {
       if (c < C) {
-        H[c] = fmaf(ds, e[c], H[c]);
+        Hn[c] = fmaf(pd, e[c], Hn[c]);
         G[c] = fmaf(P, e[c], G[c]);
       }
     }
   }
-  if (!p.use_attn_bias) sig = 0.f;  // sigma only enters dq through b
+  const float Dr = acc_p > 0.f ? acc_a / acc_p : 0.f;
+  float sig = acc_a - Dr * acc_p;
+  float dqp[kMax], H[kMax];
+#pragma unroll
+  for (int d = 0; d < kMax; ++d) {
+    dqp[d] = X[d] - Dr * Y[d];
+    H[d] = Hn[d] - Dr * G[d];
+  }
+  const float sig_out = sig;
+  if (!p.use_attn_bias) sig = 0.f;  // sigma only enters dq through b (attn)
   // dq = scale (dqp + [attn] (H W^T + sigma b))  (upstream backward.py:600-605)
   for (int d = 0; d < D; ++d) {
     float g = dqp[d];
@@ -306,8 +308,7 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
     gbuf[coff + c] = p.use_act_bias ? G[c] : 0.f;
   }
   a.delta[so] = r.off + Dr;
-  a.sigma[so] = sig;
-  if (a.ds_absmax) a.ds_absmax[so] = amax;
+  a.sigma[so] = sig_out;
 }
 
 // Column-owned backward: dk_j = sum_i dS_ij qt_i, dv_j = sum_i P_ij dO_i.
@@ -336,6 +337,8 @@ __global__ void __launch_bounds__(128) bwd_cols_kernel(FstBackwardArgs a) {
     float P, dP;
     p_dp<T>(a, r, t.row, t.h, kv, vv, e, P, dP);
     const float ds = P * (dP - (a.delta[stat_off(p, qrow, t.h)] - r.off));
+    if (a.ds_absmax)
+      atomicMax((int*)&a.ds_absmax[stat_off(p, qrow, t.h)], __float_as_int(fabsf(ds)));
 #pragma unroll
     for (int d = 0; d < kMax; ++d) {
       if (d < D) {
@@ -403,6 +406,7 @@ static int launch_bwd_t(const FstBackwardArgs& a, cudaStream_t st) {
   const int64_t n = p.total_rows * p.heads;
   float* hbuf = (float*)a.workspace;
   float* gbuf = hbuf + (size_t)n * p.channels;
+  if (a.ds_absmax) cudaMemsetAsync(a.ds_absmax, 0, (size_t)n * sizeof(float), st);
   if (n > 0) {
     const unsigned grid = (unsigned)((n + 127) / 128);
     bwd_rows_kernel<T><<<grid, 128, 0, st>>>(a, hbuf, gbuf);

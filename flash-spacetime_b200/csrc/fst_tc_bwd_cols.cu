@@ -1,0 +1,586 @@
+// Tensor-core backward, column-owned half (bf16 / fp16 inputs), sm_100a.
+//
+// Produces dk_j = sum_i dS_ij qt_i and dv_j = sum_i P_ij dO_i for the 16 keys
+// j of one event this CTA owns, for up to HP heads, looping over the event's
+// queries in chunks of 16 -- upstream's flash_spacetime_bwd_cols_kernel
+// (src/flash_spacetime/backward.py:209-313): every key row has exactly one
+// writer and the loop order is fixed, so the result is deterministic without
+// atomics. P and dS are recomputed from the saved LSE and from D written by
+// the row kernel: P_ij = exp(s_ij - lse_i), dS_ij = P_ij (dP_ij - D_i) with
+// dP_ij = dO_i . v_j + [act] w~_i . E_ij (the dO.b row constant is left out of
+// both dP and D, where it cancels).
+//
+// Orientation: keys on the MMA M axis. Head warps hold K and V of their head
+// as A fragments, compute S^T = K Q^T and dP^T = V dO^T (queries on N), and
+// accumulate dV += P^T dO and dK += dS^T Q with P^T / dS^T reused directly as
+// A fragments. E warps evaluate E_ij once per pair for all heads and form
+// the two bias products u_i . E_ij and w~_i . E_ij per query (heads on M),
+// handing them to the head warps through a double-buffered shared tile laid
+// out [head][key][query] so that each head warp reads its slice with 16-byte
+// loads.
+//
+// With ds_absmax given, the kernel also reports rowmax_j |dS_ij| per (i, h)
+// through atomicMax on the float bit pattern (max is order independent, so
+// the result is still deterministic).
+
+#include <cuda_runtime.h>
+
+#include "fst_internal.h"
+#include "fst_tc_common.cuh"
+
+namespace fst {
+namespace tc {
+
+template <int DH, int C>
+struct ColShape {
+  static constexpr int BK = 16;   // keys per CTA
+  static constexpr int BQ = 16;   // queries per chunk
+  static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1);
+  static constexpr int NE = BQ / QPE;
+  static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;
+  static constexpr int NWARPS = HP + NE;
+  static constexpr int KSD = DH / 16, NTD = DH / 8;
+  static constexpr int KSC = C / 16;
+  static constexpr int F = C / 2, FG = F / 8;
+  static constexpr int DHP = DH <= 16 ? 16 : (DH <= 32 ? 32 : 64);
+  static constexpr int CP = C <= 16 ? 16 : (C <= 32 ? 32 : 64);
+  static constexpr int RBD = DHP * 2, RBC = CP * 2;
+  // bias tile [head][key][query] of (u.E, w~.E) pairs: 32 words per key row
+  // + 16 pad so two key rows of a 16-byte load wavefront use distinct banks.
+  static constexpr int JS = 48;
+  static constexpr int HS = BK * JS;
+  static constexpr int SZ_BIAS = HP * HS * 4;                 // one stage
+  // head-warp ring stage: Q chunk, dO chunk [BQ][DHP] + lse2, delta [BQ]
+  static constexpr int SZ_HR = 2 * BQ * RBD + 2 * BQ * 4;
+  // E-warp ring stage: u and w~ rows [QPE][HP][CP] + query coords [QPE][4].
+  // The MMA's head rows past the CTA's heads read a shared zero row instead.
+  static constexpr int UW = QPE * HP * RBC;                   // one of u / w~
+  static constexpr int SZ_ER = 2 * UW + QPE * 16;
+
+  static constexpr int SZ_KVS = HP * BK * RBD;                // staged K (and V)
+  static constexpr int OFF_KS = 0, OFF_VS = SZ_KVS;           // prologue only
+  static constexpr int OFF_BIAS = 0;                          // loop: [2][HP][BK][JS]
+  static constexpr int SZ_U = (2 * SZ_KVS > 2 * SZ_BIAS) ? 2 * SZ_KVS : 2 * SZ_BIAS;
+  static constexpr int OFF_HR = SZ_U;                         // [HP][2] stages
+  static constexpr int OFF_ER = OFF_HR + HP * 2 * SZ_HR;      // [NE][2] stages
+  static constexpr int OFF_KC = OFF_ER + NE * 2 * SZ_ER;      // key coords [BK][4]
+  static constexpr int OFF_ZR = OFF_KC + BK * 16;             // zero row [CP]
+  static constexpr int SMEM = OFF_ZR + RBC;
+  static constexpr bool kFits = SMEM <= 227 * 1024;
+};
+
+__device__ __forceinline__ int cb_bias_full(int s) { return 1 + s; }
+__device__ __forceinline__ int cb_bias_empty(int s) { return 3 + s; }
+
+template <typename T, int DH, int C>
+__global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
+    bwd_cols_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
+                       int heads_per_group) {
+  using S = ColShape<DH, C>;
+  using E = Elem<T>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const FstProblem& p = a.prob;
+
+  int b, kb;
+  if (!p.packed) {
+    b = blockIdx.y;
+    kb = blockIdx.x;
+  } else {
+    const int t = blockIdx.x;
+    if (t >= tile_start[p.batch]) return;
+    int lo = 0, hi = p.batch - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+    kb = t - tile_start[b];
+  }
+  const EventSpan ev = event_span(p, b);
+  const int k0 = kb * S::BK;
+  const int h0 = blockIdx.z * heads_per_group;
+  const int NH = min(heads_per_group, p.heads - h0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NE = S::NE;
+  const int nthreads = blockDim.x;
+  const bool attn = p.use_attn_bias != 0, act = p.use_act_bias != 0;
+  const T* __restrict__ gq = (const T*)a.q;
+  const T* __restrict__ gk = (const T*)a.k;
+  const T* __restrict__ gv = (const T*)a.v;
+  const T* __restrict__ gdo = (const T*)a.dout;
+  T* __restrict__ gdk = (T*)a.dk;
+  T* __restrict__ gdv = (T*)a.dv;
+
+  if (k0 >= ev.len) {
+    if (!p.packed) {
+      for (int idx = threadIdx.x; idx < NH * S::BK; idx += nthreads) {
+        const int h = h0 + idx / S::BK, j = k0 + idx % S::BK;
+        if (j >= p.max_len) continue;
+        const int64_t off = vec_off(p, ev.row0 + j, h, DH);
+        for (int d = 0; d < DH; ++d) gdk[off + d] = gdv[off + d] = from_f<T>(0.f);
+      }
+    }
+    return;
+  }
+  const int nvalid_k = min(S::BK, ev.len - k0);
+  const int nchunks = (ev.len + S::BQ - 1) / S::BQ;
+  const int NBAR = (NH + NE) * 32;
+  const uint32_t sm = smem_u32(smem);
+  float* fKC = (float*)(smem + S::OFF_KC);
+
+  // ------------------------------ prologue ---------------------------------
+  {
+    constexpr int CH = DH / 8;
+    for (int idx = threadIdx.x; idx < NH * S::BK * CH; idx += nthreads) {
+      const int c = idx % CH, j = (idx / CH) % S::BK, h = idx / (CH * S::BK);
+      uint4 vk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      if (j < nvalid_k) {
+        const int64_t go = vec_off(p, ev.row0 + k0 + j, h0 + h, DH) + c * 8;
+        vk = *(const uint4*)(gk + go);
+        vv = *(const uint4*)(gv + go);
+      }
+      const uint32_t off = h * S::BK * S::RBD + swz<S::RBD>(j, c);
+      *(uint4*)(smem + S::OFF_KS + off) = vk;
+      *(uint4*)(smem + S::OFF_VS + off) = vv;
+    }
+    for (int idx = threadIdx.x; idx < S::BK * 4; idx += nthreads) {
+      const int j = idx / 4, k = idx % 4;
+      fKC[idx] = j < nvalid_k ? p.feats[(ev.row0 + k0 + j) * p.feat_stride + k] : 0.f;
+    }
+    for (int idx = threadIdx.x; idx < S::RBC / 4; idx += nthreads)
+      ((uint32_t*)(smem + S::OFF_ZR))[idx] = 0u;
+  }
+  __syncthreads();
+  const int m4 = lane & 3, r8 = lane >> 2;
+  const bool idle = warp >= NH + NE;
+  uint32_t ka[S::KSD][4], va[S::KSD][4];  // head warps: K, V with keys on M
+  if (warp < NH) {
+#pragma unroll
+    for (int ks = 0; ks < S::KSD; ++ks) {
+      const int mi = lane >> 3;
+      const int j = (mi & 1) * 8 + (lane & 7);
+      const uint32_t off = warp * S::BK * S::RBD + swz<S::RBD>(j, 2 * ks + (mi >> 1));
+      ldsm_x4(sm + S::OFF_KS + off, ka[ks]);
+      ldsm_x4(sm + S::OFF_VS + off, va[ks]);
+    }
+  }
+  __syncthreads();  // staging bytes become the bias tiles
+
+  if (idle) return;
+
+  if (warp >= NH) {
+    // =============================== E warps ==============================
+    const int e = warp - NH;
+    float fr[S::FG][2];
+#pragma unroll
+    for (int g = 0; g < S::FG; ++g) {
+      fr[g][0] = p.freqs[8 * g + 2 * m4];
+      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+    }
+    // Coordinates of the two keys this lane pairs with (n-tile 0 and 1).
+    Coord4 ck[2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      const int j = nt * 8 + r8;
+      ck[nt].x = fKC[j * 4 + 0];
+      ck[nt].y = fKC[j * 4 + 1];
+      ck[nt].z = fKC[j * 4 + 2];
+      ck[nt].t = fKC[j * 4 + 3];
+    }
+    const uint32_t ring = sm + S::OFF_ER + e * 2 * S::SZ_ER;
+    auto load_ring = [&](int n) {
+      if (n < nchunks) {
+        const uint32_t st = ring + (n & 1) * S::SZ_ER;
+        constexpr int CC = C / 8;  // 16-byte chunks per (q, h) row
+        for (int idx = lane; idx < S::QPE * NH * CC; idx += 32) {
+          const int c = idx % CC, h = (idx / CC) % NH, t = idx / (CC * NH);
+          const int i = n * S::BQ + e * S::QPE + t;
+          const uint32_t off = swz<S::RBC>(t * S::HP + h, c);
+          if (i < ev.len) {
+            const int64_t go = vec_off(p, ev.row0 + i, h0 + h, C) + c * 8;
+            if (attn) cp_async16(st + off, (const T*)a.u + go);
+            if (act) cp_async16(st + S::UW + off, (const T*)a.wt + go);
+          } else {
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + off), "r"(0));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + S::UW + off),
+                         "r"(0));
+          }
+        }
+        if (lane < S::QPE) {
+          const int i = n * S::BQ + e * S::QPE + lane;
+          const uint32_t dst = st + 2 * S::UW + lane * 16;
+          if (i < ev.len)
+            cp_async16(dst, p.feats + (ev.row0 + i) * p.feat_stride);
+          else
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
+        }
+      }
+      cp_async_commit();
+    };
+    load_ring(0);
+    load_ring(1);
+
+    for (int n = 0; n < nchunks; ++n) {
+      const int s = n & 1;
+      cp_async_wait<1>();
+      __syncwarp();
+      const uint32_t st = ring + s * S::SZ_ER;
+      uint32_t ua[S::QPE][S::KSC][4], wa[S::QPE][S::KSC][4];
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+        for (int ks = 0; ks < S::KSC; ++ks) {
+          const int mi = lane >> 3;
+          const int h = (mi & 1) * 8 + (lane & 7);
+          const int chunk = 2 * ks + (mi >> 1);
+          const bool real = h < NH;
+          const uint32_t au = real ? st + swz<S::RBC>(t * S::HP + h, chunk)
+                                   : sm + S::OFF_ZR + chunk * 16;
+          const uint32_t aw = real ? au + S::UW : au;
+          ldsm_x4(au, ua[t][ks]);
+          ldsm_x4(aw, wa[t][ks]);
+        }
+      // x for (query m4 of this warp, key nt*8 + r8).
+      float xl[2];
+      {
+        const int t = m4 < S::QPE ? m4 : 0;
+        const float4 c4 =
+            *(const float4*)(smem + S::OFF_ER + (e * 2 + s) * S::SZ_ER + 2 * S::UW + t * 16);
+        Coord4 cq;
+        cq.x = c4.x;
+        cq.y = c4.y;
+        cq.z = c4.z;
+        cq.t = c4.w;
+        xl[0] = pair_angle(cq, ck[0]);
+        xl[1] = pair_angle(cq, ck[1]);
+      }
+      __syncwarp();
+      load_ring(n + 2);
+
+      if (n >= 2) named_sync(cb_bias_empty(s), NBAR);
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t) {
+        float sn[2][S::FG][2], cs[2][S::FG][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+#pragma unroll
+          for (int g = 0; g < S::FG; ++g)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+        }
+        const int qq = e * S::QPE + t;  // query index within the chunk
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          uint32_t eb[S::KSC][2];
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks)
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+              const int cb = 16 * ks + 8 * hi;
+              const int g = (cb % S::F) / 8;
+              const bool is_sin = cb < S::F;
+              eb[ks][hi] = E::pack(is_sin ? sn[nt][g][0] : cs[nt][g][0],
+                                   is_sin ? sn[nt][g][1] : cs[nt][g][1]);
+            }
+          float du[4] = {0.f, 0.f, 0.f, 0.f}, dw[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks) {
+            if (attn) mma16816<T>(du, ua[t][ks], eb[ks]);
+            if (act) mma16816<T>(dw, wa[t][ks], eb[ks]);
+          }
+          // D[h][key]: h = r8 (+8), keys nt*8 + 2 m4 (+1). Tile [h][key][q].
+          const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS + (2 * qq) * 4;
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            const int j = nt * 8 + 2 * m4 + r;
+            if (r8 < NH) sts_v2(base + (r8 * S::HS + j * S::JS) * 4, du[r], dw[r]);
+            if (r8 + 8 < NH) sts_v2(base + ((r8 + 8) * S::HS + j * S::JS) * 4, du[2 + r], dw[2 + r]);
+          }
+        }
+      }
+      named_arrive(cb_bias_full(s), NBAR);
+    }
+    return;
+  }
+
+  // ================================ head warps ===============================
+  const int hl = warp;
+  const int h = h0 + hl;
+  const uint32_t ring = sm + S::OFF_HR + hl * 2 * S::SZ_HR;
+  auto load_ring = [&](int n) {
+    if (n < nchunks) {
+      const uint32_t st = ring + (n & 1) * S::SZ_HR;
+      constexpr int CH = DH / 8;
+      for (int idx = lane; idx < S::BQ * CH; idx += 32) {
+        const int c = idx % CH, i = idx / CH;
+        const uint32_t off = swz<S::RBD>(i, c);
+        const int qi = n * S::BQ + i;
+        if (qi < ev.len) {
+          const int64_t go = vec_off(p, ev.row0 + qi, h, DH) + c * 8;
+          cp_async16(st + off, gq + go);
+          cp_async16(st + S::BQ * S::RBD + off, gdo + go);
+        } else {
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + off), "r"(0));
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + S::BQ * S::RBD + off),
+                       "r"(0));
+        }
+      }
+      if (lane < S::BQ) {
+        const int qi = n * S::BQ + lane;
+        float l2 = 0.f, dl = 0.f;
+        if (qi < ev.len) {
+          const int64_t so = stat_off(p, ev.row0 + qi, h);
+          l2 = a.lse[so] * kLog2e;
+          dl = a.delta[so];
+        }
+        float* f = (float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
+        f[lane] = l2;
+        f[S::BQ + lane] = dl;
+      }
+    }
+    cp_async_commit();
+  };
+  load_ring(0);
+  load_ring(1);
+
+  float dk[S::NTD][4], dv[S::NTD][4];
+#pragma unroll
+  for (int nd = 0; nd < S::NTD; ++nd)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) dk[nd][i] = dv[nd][i] = 0.f;
+
+  for (int n = 0; n < nchunks; ++n) {
+    const int s = n & 1;
+    const int i0 = n * S::BQ;
+    cp_async_wait<1>();
+    __syncwarp();
+    const uint32_t st = ring + s * S::SZ_HR;
+    const uint32_t q_st = st, do_st = st + S::BQ * S::RBD;
+    // qt = [q * scale], in place: each lane rescales the chunks it copied.
+    {
+      constexpr int CH = DH / 8;
+      for (int idx = lane; idx < S::BQ * CH; idx += 32) {
+        const int c = idx % CH, i = idx / CH;
+        uint4* ptr = (uint4*)(smem + (q_st - sm) + swz<S::RBD>(i, c));
+        uint4 v = *ptr;
+        uint32_t* w = (uint32_t*)&v;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) w[k] = E::pack(E::lo(w[k]) * p.scale, E::hi(w[k]) * p.scale);
+        *ptr = v;
+      }
+    }
+    __syncwarp();
+    const float* stat = (const float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
+
+    // S^T = K Q^T, dP^T = V dO^T (B fragments: k = head dim, n = query).
+    float sc[2][4], dp[2][4];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) sc[nt][i] = dp[nt][i] = 0.f;
+#pragma unroll
+      for (int kp = 0; kp < (S::KSD + 1) / 2; ++kp) {
+        const int mi = lane >> 3;
+        uint32_t rq[4], rd[4];
+        if (S::KSD - 2 * kp >= 2) {
+          const uint32_t off = swz<S::RBD>(nt * 8 + (lane & 7), 4 * kp + mi);
+          ldsm_x4(q_st + off, rq);
+          ldsm_x4(do_st + off, rd);
+          mma16816<T>(sc[nt], ka[2 * kp], rq);
+          mma16816<T>(sc[nt], ka[2 * kp + 1], rq + 2);
+          mma16816<T>(dp[nt], va[2 * kp], rd);
+          mma16816<T>(dp[nt], va[2 * kp + 1], rd + 2);
+        } else {
+          const uint32_t off = swz<S::RBD>(nt * 8 + (lane & 7), 4 * kp + (mi & 1));
+          ldsm_x2(q_st + off, rq);
+          ldsm_x2(do_st + off, rd);
+          mma16816<T>(sc[nt], ka[2 * kp], rq);
+          mma16816<T>(dp[nt], va[2 * kp], rd);
+        }
+      }
+    }
+    named_sync(cb_bias_full(s), NBAR);
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      // keys r8 (+8), queries nt*8 + 2 m4 (+1): (u, w) pairs, 16 bytes per key.
+      const uint32_t base =
+          sm + S::OFF_BIAS + s * S::SZ_BIAS + (hl * S::HS + 2 * (nt * 8 + 2 * m4)) * 4;
+      float4 b0, b1;
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                   : "=f"(b0.x), "=f"(b0.y), "=f"(b0.z), "=f"(b0.w)
+                   : "r"(base + r8 * S::JS * 4));
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                   : "=f"(b1.x), "=f"(b1.y), "=f"(b1.z), "=f"(b1.w)
+                   : "r"(base + (r8 + 8) * S::JS * 4));
+      sc[nt][0] += b0.x;
+      dp[nt][0] += b0.y;
+      sc[nt][1] += b0.z;
+      dp[nt][1] += b0.w;
+      sc[nt][2] += b1.x;
+      dp[nt][2] += b1.y;
+      sc[nt][3] += b1.z;
+      dp[nt][3] += b1.w;
+    }
+    if (n + 2 < nchunks) named_arrive(cb_bias_empty(s), NBAR);
+
+    // P^T and dS^T; queries past the event (last chunk) get P = 0.
+    uint32_t pt[4], dt[4];
+    float amax[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [nt][column pair member]
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int qi = nt * 8 + 2 * m4 + (i & 1);
+        float pv = ex2(fmaf(sc[nt][i], kLog2e, -stat[qi]));
+        if (i0 + qi >= ev.len) pv = 0.f;
+        const float ds = pv * (dp[nt][i] - stat[S::BQ + qi]);
+        sc[nt][i] = pv;
+        dp[nt][i] = ds;
+        if ((i >> 1) == 0 ? (r8 < nvalid_k) : (r8 + 8 < nvalid_k))
+          amax[nt][i & 1] = fmaxf(amax[nt][i & 1], fabsf(ds));
+      }
+    pt[0] = E::pack(sc[0][0], sc[0][1]);
+    pt[1] = E::pack(sc[0][2], sc[0][3]);
+    pt[2] = E::pack(sc[1][0], sc[1][1]);
+    pt[3] = E::pack(sc[1][2], sc[1][3]);
+    dt[0] = E::pack(dp[0][0], dp[0][1]);
+    dt[1] = E::pack(dp[0][2], dp[0][3]);
+    dt[2] = E::pack(dp[1][0], dp[1][1]);
+    dt[3] = E::pack(dp[1][2], dp[1][3]);
+    if (a.ds_absmax) {
+      // max over this warp's 16 keys (lanes with equal m4), then one atomic
+      // per (query, head) from the r8 == 0 lanes.
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int c = 0; c < 2; ++c) {
+          float v = amax[nt][c];
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
+          v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
+          const int qi = i0 + nt * 8 + 2 * m4 + c;
+          if (r8 == 0 && qi < ev.len)
+            atomicMax((int*)&a.ds_absmax[stat_off(p, ev.row0 + qi, h)], __float_as_int(v));
+        }
+    }
+    // dV += P^T dO, dK += dS^T qt (B fragments: k = query, n = head dim).
+#pragma unroll
+    for (int np = 0; np < (S::NTD + 1) / 2; ++np) {
+      const int mi = lane >> 3;
+      uint32_t rdo[4], rq[4];
+      if (S::NTD - 2 * np >= 2) {
+        const uint32_t off = swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np + (mi >> 1));
+        ldsm_x4_t(do_st + off, rdo);
+        ldsm_x4_t(q_st + off, rq);
+        mma16816<T>(dv[2 * np], pt, rdo);
+        mma16816<T>(dv[2 * np + 1], pt, rdo + 2);
+        mma16816<T>(dk[2 * np], dt, rq);
+        mma16816<T>(dk[2 * np + 1], dt, rq + 2);
+      } else {
+        const uint32_t off = swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np);
+        ldsm_x2_t(do_st + off, rdo);
+        ldsm_x2_t(q_st + off, rq);
+        mma16816<T>(dv[2 * np], pt, rdo);
+        mma16816<T>(dk[2 * np], dt, rq);
+      }
+    }
+    __syncwarp();
+    load_ring(n + 2);
+  }
+
+#pragma unroll
+  for (int rh = 0; rh < 2; ++rh) {
+    const int j = r8 + 8 * rh;
+    const bool valid = j < nvalid_k;
+    if (!valid && (p.packed || k0 + j >= p.max_len)) continue;
+    const int64_t off = vec_off(p, ev.row0 + k0 + j, h, DH);
+#pragma unroll
+    for (int nd = 0; nd < S::NTD; ++nd) {
+      const int d = nd * 8 + 2 * m4;
+      *(uint32_t*)(gdk + off + d) =
+          valid ? E::pack(dk[nd][2 * rh], dk[nd][2 * rh + 1]) : 0u;
+      *(uint32_t*)(gdv + off + d) =
+          valid ? E::pack(dv[nd][2 * rh], dv[nd][2 * rh + 1]) : 0u;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+template <typename T, int DH, int C>
+static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
+  using S = ColShape<DH, C>;
+  const FstProblem& p = a.prob;
+  if constexpr (!S::kFits) {
+    return FST_ERR_UNSUPPORTED;
+  } else {
+    static bool configured = false;
+    if (!configured) {
+      if (cudaFuncSetAttribute(bwd_cols_tc_kernel<T, DH, C>,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               S::SMEM) != cudaSuccess)
+        return FST_ERR_CUDA;
+      configured = true;
+    }
+    const int groups = (p.heads + S::HP - 1) / S::HP;
+    const int per_group = (p.heads + groups - 1) / groups;
+    const int threads = (per_group + S::NE) * 32;
+    dim3 grid;
+    if (p.packed) {
+      // tile_start (16-row tiles) was built by the row kernel's launch.
+      const int64_t upper = (p.total_rows + S::BK - 1) / S::BK + p.batch;
+      grid = dim3((unsigned)upper, 1, groups);
+    } else {
+      grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
+    }
+    if (grid.x == 0 || grid.y == 0) return FST_OK;
+    bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group);
+    count_launch();
+    return FST_OK;
+  }
+}
+
+template <typename T>
+static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
+  const int D = a.prob.head_dim, C = a.prob.channels;
+#define FST_COLS_CASE(DD, CC) \
+  if (D == DD && C == CC) return launch_cols_shape<T, DD, CC>(a, st, ts);
+  FST_COLS_CASE(32, 16)
+  FST_COLS_CASE(32, 32)
+  FST_COLS_CASE(32, 64)
+  FST_COLS_CASE(64, 32)
+  FST_COLS_CASE(64, 64)
+  FST_COLS_CASE(16, 16)
+  FST_COLS_CASE(48, 48)
+#undef FST_COLS_CASE
+  return FST_ERR_UNSUPPORTED;
+}
+
+int launch_bwd_cols(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
+  if (a.prob.dtype == FST_BF16) return launch_cols_t<__nv_bfloat16>(a, st, tile_start);
+  if (a.prob.dtype == FST_F16) return launch_cols_t<__half>(a, st, tile_start);
+  return FST_ERR_UNSUPPORTED;
+}
+
+bool bwd_supported(const FstProblem& p) {
+  return fwd_supported(p);  // same (Dh, C) list; every shape fits both kernels
+}
+
+size_t bwd_workspace(const FstProblem& p) {
+  return (size_t)(p.batch + 1) * sizeof(int) + 64;
+}
+
+int launch_bwd(const FstBackwardArgs& a, cudaStream_t st) {
+  int* tile_start = (int*)a.workspace + 16;
+  if (a.ds_absmax) {
+    const int64_t n = a.prob.total_rows * a.prob.heads;
+    if (cudaMemsetAsync(a.ds_absmax, 0, n * sizeof(float), st) != cudaSuccess) return FST_ERR_CUDA;
+  }
+  int rc = launch_bwd_rows(a, st, tile_start);
+  if (rc) return rc;
+  return launch_bwd_cols(a, st, tile_start);
+}
+
+}  // namespace tc
+}  // namespace fst

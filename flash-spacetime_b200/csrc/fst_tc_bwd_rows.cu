@@ -1,0 +1,776 @@
+// Tensor-core backward, row-owned half (bf16 / fp16 inputs), sm_100a.
+//
+// Produces, per query row i and head h: dq (with upstream's host epilogue
+// dq = scale (dqp + H W^T + sigma b) fused, backward.py:600-605), D, sigma =
+// rowsum(dS) and this CTA's partial of dW = sum qt (x) H + dO (x) G
+// (backward.py:607-614). Upstream computes the same quantities in
+// flash_spacetime_bwd_rows_kernel (backward.py:316-485) with two sweeps over
+// the keys: one for D = sum P dP / sum P, one for dS = P (dP - D).
+//
+// Here a single sweep suffices. With c_i = dO_i . (out_i - [act] b) (an
+// estimate of D from the forward output) and dP'_ij = dP_ij - c_i, the
+// sweep accumulates, from the rounded operands that the tensor cores see,
+//   X_i  = sum_j [P dP']_ij k_j       Y_i  = sum_j [P]_ij k_j
+//   H'_i = sum_j [P dP']_ij E_ij      G_i  = sum_j [P]_ij E_ij
+//   a_i  = sum_j [P dP']_ij           p_i  = sum_j [P]_ij
+// ([.] = rounded to the 16-bit type), and at the end
+//   D'_i = a_i / p_i,   dqp_i = X_i - D'_i Y_i,   H_i = H'_i - D'_i G_i,
+//   sigma_i = a_i - D'_i p_i.
+// This is dS_ij = [P dP']_ij - D'_i [P]_ij contracted exactly: every sum of
+// dS that feeds dq, H and sigma is formed from the same rounded values, so
+// rowsum(dS) = a - D' p vanishes up to one fp32 rounding, and D = c + D' is
+// the P-weighted mean of dP normalised by sum P as upstream requires
+// (backward.py:371-407). Subtracting c first keeps the row's common mode out
+// of the 16-bit products.
+//
+// Layout and warp roles follow the forward kernel (fst_tc_fwd.cu): head
+// warps own one head's 16 rows (S = Q K^T, dP = dO V^T, X, Y on the tensor
+// cores), E warps own QPE rows for all heads (embedding, the two logit-side
+// bias products u.E and w~.E, and H', G), and the per-chunk bias tiles and P
+// tiles cross between the two groups through double-buffered shared memory.
+
+#include <cuda_runtime.h>
+
+#include "fst_internal.h"
+#include "fst_tc_common.cuh"
+
+namespace fst {
+namespace tc {
+
+template <int DH, int C>
+struct RowShape {
+  static constexpr int BM = 16, BN = 16;
+  static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1);
+  static constexpr int NE = BM / QPE;
+  static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;  // heads per CTA
+  static constexpr int NWARPS = HP + NE;
+  static constexpr int KSD = DH / 16, NTD = DH / 8;
+  static constexpr int KSC = C / 16, NTC = C / 8;
+  static constexpr int F = C / 2, FG = F / 8;
+  static constexpr int DHP = DH <= 16 ? 16 : (DH <= 32 ? 32 : 64);
+  static constexpr int CP = C <= 16 ? 16 : (C <= 32 ? 32 : 64);
+  static constexpr int RBD = DHP * 2, RBC = CP * 2;
+  // bias tile: per (q, h) 16 keys x (u.E, w~.E) fp32 + 16 pad words.
+  static constexpr int BROW = 48;
+  static constexpr int BQ = HP * BROW + 16;
+  static constexpr int PQ = 16 * 8 + 4;  // P tile words per query (16 heads x 16 keys)
+
+  // The union region holds, in turn: staged Q and dO (phase 1), staged u and
+  // w~ (phase 2), the loop's bias and P tiles, and the epilogue's H and G.
+  // The epilogue's R = H W^T goes to the K/V ring, dead by then.
+  static constexpr int SZ_QS = HP * BM * RBD;     // staged Q (scaled), and dO
+  static constexpr int SZ_US = BM * 16 * RBC;     // staged u, and w~
+  static constexpr int SZ_B = BM * BQ * 4;        // one bias stage
+  static constexpr int SZ_P = BM * PQ * 4;        // one P tile
+  static constexpr int SZ_LOOP = 2 * SZ_B + 4 * SZ_P;  // bias x2, (P, P dP') x2
+  static constexpr int SZ_HG = 2 * BM * HP * C * 4;
+  static constexpr int SZ_A = 2 * SZ_QS > 2 * SZ_US ? 2 * SZ_QS : 2 * SZ_US;
+  static constexpr int SZ_B2 = SZ_LOOP > SZ_HG ? SZ_LOOP : SZ_HG;
+  static constexpr int SZ_UNION = SZ_A > SZ_B2 ? SZ_A : SZ_B2;
+  static constexpr int OFF_Q = 0, OFF_DO = SZ_QS, OFF_U = 0, OFF_WT = SZ_US;
+  static constexpr int OFF_B = 0, OFF_P = 2 * SZ_B;
+  static constexpr int OFF_H = 0, OFF_G = BM * HP * C * 4;
+  static constexpr int OFF_W = SZ_UNION;
+  static constexpr int SZ_W = 2 * DH * RBC;
+  static constexpr int OFF_K = OFF_W + SZ_W;
+  static constexpr int SZ_KV = HP * BN * RBD;
+  static constexpr int OFF_V = OFF_K + 2 * SZ_KV;
+  static constexpr int OFF_C = OFF_V + 2 * SZ_KV;           // [NE][2][BN][4]
+  static constexpr int OFF_QC = OFF_C + NE * 2 * BN * 16;   // [BM][4]
+  static constexpr int OFF_ST = OFF_QC + BM * 16;           // lse2, coff, D' : [3][BM][HP]
+  static constexpr int SMEM = OFF_ST + 3 * BM * HP * 4;
+  static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
+  static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
+  static constexpr bool kFits = SMEM <= 227 * 1024;
+};
+
+__device__ __forceinline__ int rb_bias_full(int s) { return 1 + s; }
+__device__ __forceinline__ int rb_bias_empty(int s) { return 3 + s; }
+__device__ __forceinline__ int rb_p_full(int s) { return 5 + s; }
+__device__ __forceinline__ int rb_p_empty(int s) { return 7 + s; }
+
+template <typename T, int DH, int C>
+__global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
+    bwd_rows_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
+                       int heads_per_group, int n_row_tiles) {
+  using S = RowShape<DH, C>;
+  using E = Elem<T>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  const FstProblem& p = a.prob;
+
+  int b, qb;
+  if (!p.packed) {
+    b = blockIdx.y;
+    qb = blockIdx.x;
+  } else {
+    const int t = blockIdx.x;
+    if (t >= tile_start[p.batch]) {
+      // Beyond the tile list: this CTA's dW partial slot still needs zeros.
+      const int64_t part = (int64_t)blockIdx.z * gridDim.x + blockIdx.x;
+      for (int i = threadIdx.x; i < DH * C; i += blockDim.x)
+        a.dw_partial[part * DH * C + i] = 0.f;
+      return;
+    }
+    int lo = 0, hi = p.batch - 1;
+    while (lo < hi) {
+      int mid = (lo + hi + 1) >> 1;
+      if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    b = lo;
+    qb = t - tile_start[b];
+  }
+  const int64_t part = p.packed ? ((int64_t)blockIdx.z * gridDim.x + blockIdx.x)
+                                : (((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x +
+                                   blockIdx.x);
+  float* dwp = a.dw_partial + part * DH * C;
+  const EventSpan ev = event_span(p, b);
+  const int q0 = qb * S::BM;
+  const int h0 = blockIdx.z * heads_per_group;
+  const int NH = min(heads_per_group, p.heads - h0);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int NE = S::NE;
+  const int nthreads = blockDim.x;
+  const bool attn = p.use_attn_bias != 0, act = p.use_act_bias != 0;
+  const T* __restrict__ gq = (const T*)a.q;
+  const T* __restrict__ gk = (const T*)a.k;
+  const T* __restrict__ gv = (const T*)a.v;
+  const T* __restrict__ gdo = (const T*)a.dout;
+  const T* __restrict__ gout = (const T*)a.out;
+  T* __restrict__ gdq = (T*)a.dq;
+
+  if (q0 >= ev.len) {
+    for (int i = threadIdx.x; i < DH * C; i += nthreads) dwp[i] = 0.f;
+    if (!p.packed) {
+      for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
+        const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
+        if (q >= p.max_len) continue;
+        const int64_t row = ev.row0 + q;
+        T* o = gdq + vec_off(p, row, h, DH);
+        for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
+        const int64_t so = stat_off(p, row, h);
+        a.delta[so] = 0.f;
+        a.sigma[so] = 0.f;
+      }
+    }
+    return;
+  }
+  const int nvalid_q = min(S::BM, ev.len - q0);
+  const int nchunks = (ev.len + S::BN - 1) / S::BN;
+  const int NBAR = (NH + NE) * 32;
+  const uint32_t sm = smem_u32(smem);
+  float* fQC = (float*)(smem + S::OFF_QC);
+  float* fLse = (float*)(smem + S::OFF_ST);
+  float* fCoff = fLse + S::BM * S::HP;
+  float* fDp = fCoff + S::BM * S::HP;
+
+  // ------------------------------- prologue -------------------------------
+  {
+    constexpr int QCH = DH / 8;
+    for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
+      const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
+      uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
+      if (q < nvalid_q) {
+        const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8;
+        const uint4 raw = *(const uint4*)(gq + go);
+        vd = *(const uint4*)(gdo + go);
+        const uint32_t* w = (const uint32_t*)&raw;
+        uint32_t* o = (uint32_t*)&vq;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) o[i] = E::pack(E::lo(w[i]) * p.scale, E::hi(w[i]) * p.scale);
+      }
+      const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
+      *(uint4*)(smem + S::OFF_Q + off) = vq;
+      *(uint4*)(smem + S::OFF_DO + off) = vd;
+    }
+  }
+  __syncthreads();
+  const int m4 = lane & 3, r8 = lane >> 2;
+  const bool idle = warp >= NH + NE;
+  uint32_t qa[S::KSD][4], da[S::KSD][4];  // head warps: Q (scaled) and dO, rows on M
+  uint32_t ua[S::QPE][S::KSC][4], wa[S::QPE][S::KSC][4];  // E warps: u_q, w~_q
+  if (warp < NH) {
+#pragma unroll
+    for (int ks = 0; ks < S::KSD; ++ks) {
+      const int mi = lane >> 3;
+      const int q = (mi & 1) * 8 + (lane & 7);
+      const uint32_t off = warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1));
+      ldsm_x4(sm + S::OFF_Q + off, qa[ks]);
+      ldsm_x4(sm + S::OFF_DO + off, da[ks]);
+    }
+  }
+  __syncthreads();  // phase 2 of the staging reuses the Q / dO bytes
+  {
+    constexpr int UCH = S::CP / 8;
+    for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
+      const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
+      uint4 vu = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
+      if (q < nvalid_q && h < NH && c * 8 < C) {
+        const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8;
+        if (attn) vu = *(const uint4*)((const T*)a.u + go);
+        if (act) vw = *(const uint4*)((const T*)a.wt + go);
+      }
+      const uint32_t off = swz<S::RBC>(q * 16 + h, c);
+      *(uint4*)(smem + S::OFF_U + off) = vu;
+      *(uint4*)(smem + S::OFF_WT + off) = vw;
+    }
+    for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
+      const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
+      float w0 = 0.f, w1 = 0.f;
+      if (attn && 2 * c2 < C) {
+        w0 = p.weight[(int64_t)d * C + 2 * c2];
+        w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
+      }
+      const uint32_t hi = E::pack(w0, w1);
+      const uint32_t lo = E::pack(w0 - E::lo(hi), w1 - E::hi(hi));
+      const uint32_t off = swz<S::RBC>(d, c2 / 4) + (c2 % 4) * 4;
+      *(uint32_t*)(smem + S::OFF_W + off) = hi;
+      *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
+    }
+    for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
+      const int q = idx / 4, k = idx % 4;
+      fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
+    }
+    // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b).
+    for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
+      const int q = idx / NH, h = idx % NH;
+      float l2 = 0.f, c = 0.f;
+      if (q < nvalid_q) {
+        const int64_t row = ev.row0 + q0 + q;
+        l2 = a.lse[stat_off(p, row, h0 + h)] * kLog2e;
+        if (gout) {
+          const int64_t go = vec_off(p, row, h0 + h, DH);
+          for (int d = 0; d < DH; ++d) {
+            float od = to_f<T>(gout[go + d]);
+            if (act && p.bias) od -= p.bias[d];
+            c = fmaf(to_f<T>(gdo[go + d]), od, c);
+          }
+        }
+      }
+      fLse[q * S::HP + h] = l2;
+      fCoff[q * S::HP + h] = c;
+    }
+  }
+  __syncthreads();
+  if (warp >= NH && !idle) {
+    const int qe = (warp - NH) * S::QPE;
+#pragma unroll
+    for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+      for (int ks = 0; ks < S::KSC; ++ks) {
+        const int mi = lane >> 3;
+        const int h = (mi & 1) * 8 + (lane & 7);
+        const uint32_t off = swz<S::RBC>((qe + t) * 16 + h, 2 * ks + (mi >> 1));
+        ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
+        ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+      }
+  }
+  __syncthreads();
+  for (int idx = threadIdx.x; idx < 4 * S::SZ_P / 4; idx += nthreads)
+    ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+  __syncthreads();
+
+  if (idle) {
+    __syncthreads();
+    __syncthreads();
+    __syncthreads();
+    return;
+  }
+
+  if (warp >= NH) {
+    // =============================== E warps ==============================
+    const int e = warp - NH;
+    const int qe = e * S::QPE;
+    float fr[S::FG][2];
+#pragma unroll
+    for (int g = 0; g < S::FG; ++g) {
+      fr[g][0] = p.freqs[8 * g + 2 * m4];
+      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+    }
+    const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
+    Coord4 cq;
+    cq.x = fQC[qx_row * 4 + 0];
+    cq.y = fQC[qx_row * 4 + 1];
+    cq.z = fQC[qx_row * 4 + 2];
+    cq.t = fQC[qx_row * 4 + 3];
+    const uint32_t c_ring = sm + S::OFF_C + e * 2 * S::BN * 16;
+    auto load_coords = [&](int n) {
+      if (n < nchunks && lane < S::BN) {
+        const int j = n * S::BN + lane;
+        const uint32_t dst = c_ring + ((n & 1) * S::BN + lane) * 16;
+        if (j < ev.len)
+          cp_async16(dst, p.feats + (ev.row0 + j) * p.feat_stride);
+        else
+          asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
+      }
+      cp_async_commit();
+    };
+    load_coords(0);
+    load_coords(1);
+
+    float hacc[S::QPE][S::NTC][4], gacc[S::QPE][S::NTC][4];
+#pragma unroll
+    for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+      for (int nc = 0; nc < S::NTC; ++nc)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) hacc[t][nc][i] = gacc[t][nc][i] = 0.f;
+
+    for (int n = 0; n < nchunks; ++n) {
+      const int s = n & 1;
+      cp_async_wait<1>();
+      __syncwarp();
+      float xl[2];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const float4 ck =
+            *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + nt * 8 + r8) * 16);
+        Coord4 c4;
+        c4.x = ck.x;
+        c4.y = ck.y;
+        c4.z = ck.z;
+        c4.t = ck.w;
+        xl[nt] = pair_angle(cq, c4);
+      }
+      __syncwarp();
+      load_coords(n + 2);
+
+      uint32_t eb[S::QPE][2][S::KSC][2];
+      if (n >= 2) named_sync(rb_bias_empty(s), NBAR);
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t) {
+        float sn[2][S::FG][2], cs[2][S::FG][2];
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+#pragma unroll
+          for (int g = 0; g < S::FG; ++g)
+#pragma unroll
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+        }
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks)
+#pragma unroll
+            for (int hi = 0; hi < 2; ++hi) {
+              const int cb = 16 * ks + 8 * hi;
+              const int g = (cb % S::F) / 8;
+              const bool is_sin = cb < S::F;
+              eb[t][nt][ks][hi] = E::pack(is_sin ? sn[nt][g][0] : cs[nt][g][0],
+                                          is_sin ? sn[nt][g][1] : cs[nt][g][1]);
+            }
+        const int q = qe + t;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt) {
+          float du[4] = {0.f, 0.f, 0.f, 0.f}, dw[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks) {
+            if (attn) mma16816<T>(du, ua[t][ks], eb[t][nt][ks]);
+            if (act) mma16816<T>(dw, wa[t][ks], eb[t][nt][ks]);
+          }
+          // (u.E, w~.E) pairs for keys 2 m4 and 2 m4 + 1 of this 8-key tile.
+          const uint32_t base = sm + S::OFF_B + s * S::SZ_B + (q * S::BQ + nt * 16 + 4 * m4) * 4;
+          if (r8 < NH)
+            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(base + r8 * S::BROW * 4),
+                         "f"(du[0]), "f"(dw[0]), "f"(du[1]), "f"(dw[1]));
+          if (r8 + 8 < NH)
+            asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(base + (r8 + 8) * S::BROW * 4),
+                         "f"(du[2]), "f"(dw[2]), "f"(du[3]), "f"(dw[3]));
+        }
+      }
+      named_arrive(rb_bias_full(s), NBAR);
+
+      named_sync(rb_p_full(s), NBAR);
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t) {
+        const int q = qe + t;
+        uint32_t pp[4], pd[4];
+        const int mi = lane >> 3;
+        const int h = (mi & 1) * 8 + (lane & 7);
+        const uint32_t po = (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4;
+        ldsm_x4(sm + S::OFF_P + (2 * s) * S::SZ_P + po, pp);
+        ldsm_x4(sm + S::OFF_P + (2 * s + 1) * S::SZ_P + po, pd);
+#pragma unroll
+        for (int nc = 0; nc < S::NTC; ++nc) {
+          uint32_t bt[2];
+          bt[0] = movm_t(eb[t][0][nc >> 1][nc & 1]);
+          bt[1] = movm_t(eb[t][1][nc >> 1][nc & 1]);
+          // G is needed for dW when the output term is on, and for the
+          // D' correction of H when the logit term is on.
+          mma16816<T>(gacc[t][nc], pp, bt);
+          if (attn) mma16816<T>(hacc[t][nc], pd, bt);
+        }
+      }
+      if (n + 2 < nchunks) named_arrive(rb_p_empty(s), NBAR);
+    }
+
+    __syncthreads();  // (A) head warps published D'
+    // H = H' - D' G, stored fp32 [q][h][c] with G for the dW partial; then
+    // R = H W^T (hi/lo split of both H and W) into [q][h][d].
+    float* fH = (float*)(smem + S::OFF_H);
+    float* fG = (float*)(smem + S::OFF_G);
+    float* fR = (float*)(smem + S::OFF_R);  // K/V ring, dead after the loop
+#pragma unroll
+    for (int t = 0; t < S::QPE; ++t) {
+      const int q = qe + t;
+      const float d0 = r8 < NH ? fDp[q * S::HP + r8] : 0.f;
+      const float d1 = r8 + 8 < NH ? fDp[q * S::HP + r8 + 8] : 0.f;
+#pragma unroll
+      for (int nc = 0; nc < S::NTC; ++nc) {
+        hacc[t][nc][0] -= d0 * gacc[t][nc][0];
+        hacc[t][nc][1] -= d0 * gacc[t][nc][1];
+        hacc[t][nc][2] -= d1 * gacc[t][nc][2];
+        hacc[t][nc][3] -= d1 * gacc[t][nc][3];
+        const int c = nc * 8 + 2 * m4;
+        if (r8 < NH) {
+          fH[(q * S::HP + r8) * C + c] = hacc[t][nc][0];
+          fH[(q * S::HP + r8) * C + c + 1] = hacc[t][nc][1];
+          fG[(q * S::HP + r8) * C + c] = gacc[t][nc][0];
+          fG[(q * S::HP + r8) * C + c + 1] = gacc[t][nc][1];
+        }
+        if (r8 + 8 < NH) {
+          fH[(q * S::HP + r8 + 8) * C + c] = hacc[t][nc][2];
+          fH[(q * S::HP + r8 + 8) * C + c + 1] = hacc[t][nc][3];
+          fG[(q * S::HP + r8 + 8) * C + c] = gacc[t][nc][2];
+          fG[(q * S::HP + r8 + 8) * C + c + 1] = gacc[t][nc][3];
+        }
+      }
+      if (attn) {
+        uint32_t ah[S::KSC][4], al[S::KSC][4];
+#pragma unroll
+        for (int ks = 0; ks < S::KSC; ++ks) {
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            const float* hv = hacc[t][2 * ks + half];
+            const uint32_t h01 = E::pack(hv[0], hv[1]);
+            const uint32_t h23 = E::pack(hv[2], hv[3]);
+            ah[ks][2 * half] = h01;
+            ah[ks][2 * half + 1] = h23;
+            al[ks][2 * half] = E::pack(hv[0] - E::lo(h01), hv[1] - E::hi(h01));
+            al[ks][2 * half + 1] = E::pack(hv[2] - E::lo(h23), hv[3] - E::hi(h23));
+          }
+        }
+#pragma unroll
+        for (int nd = 0; nd < S::NTD; ++nd) {
+          float d[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks) {
+            uint32_t wh[2], wl[2];
+            const int mi = (lane >> 3) & 1;
+            const uint32_t wo = swz<S::RBC>(nd * 8 + (lane & 7), 2 * ks + mi);
+            ldsm_x2(sm + S::OFF_W + wo, wh);
+            ldsm_x2(sm + S::OFF_W + DH * S::RBC + wo, wl);
+            mma16816<T>(d, ah[ks], wh);
+            mma16816<T>(d, ah[ks], wl);
+            mma16816<T>(d, al[ks], wh);
+          }
+          const int dd = nd * 8 + 2 * m4;
+          if (r8 < NH) {
+            fR[(q * S::HP + r8) * DH + dd] = d[0];
+            fR[(q * S::HP + r8) * DH + dd + 1] = d[1];
+          }
+          if (r8 + 8 < NH) {
+            fR[(q * S::HP + r8 + 8) * DH + dd] = d[2];
+            fR[(q * S::HP + r8 + 8) * DH + dd + 1] = d[3];
+          }
+        }
+      }
+    }
+  } else {
+    // ============================== head warps ============================
+    const int hl = warp;
+    const int h = h0 + hl;
+    const uint32_t k_ring = sm + S::OFF_K + hl * S::BN * S::RBD;
+    const uint32_t v_ring = sm + S::OFF_V + hl * S::BN * S::RBD;
+    auto load_kv = [&](int n) {
+      if (n < nchunks) {
+        constexpr int CH = DH / 8;
+        const int j0 = n * S::BN;
+        const uint32_t ks_ = k_ring + (n & 1) * S::SZ_KV, vs_ = v_ring + (n & 1) * S::SZ_KV;
+        for (int idx = lane; idx < S::BN * CH; idx += 32) {
+          const int c = idx % CH, j = idx / CH;
+          const uint32_t off = swz<S::RBD>(j, c);
+          if (j0 + j < ev.len) {
+            const int64_t go = vec_off(p, ev.row0 + j0 + j, h, DH) + c * 8;
+            cp_async16(ks_ + off, gk + go);
+            cp_async16(vs_ + off, gv + go);
+          } else {
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(ks_ + off), "r"(0));
+            asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(vs_ + off), "r"(0));
+          }
+        }
+      }
+      cp_async_commit();
+    };
+    load_kv(0);
+    load_kv(1);
+    const float lse0 = fLse[r8 * S::HP + hl], lse1 = fLse[(r8 + 8) * S::HP + hl];
+    const float c0 = fCoff[r8 * S::HP + hl], c1 = fCoff[(r8 + 8) * S::HP + hl];
+    float X[S::NTD][4], Y[S::NTD][4];
+#pragma unroll
+    for (int nd = 0; nd < S::NTD; ++nd)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) X[nd][i] = Y[nd][i] = 0.f;
+    float asum[2] = {0.f, 0.f}, psum[2] = {0.f, 0.f};
+
+    for (int n = 0; n < nchunks; ++n) {
+      const int s = n & 1;
+      const int j0 = n * S::BN;
+      cp_async_wait<1>();
+      __syncwarp();
+      const uint32_t k_st = k_ring + s * S::SZ_KV, v_st = v_ring + s * S::SZ_KV;
+      // S = Q K^T and dP = dO V^T (B fragments: k = head dim, n = key).
+      float sc[2][4], dp[2][4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) sc[nt][i] = dp[nt][i] = 0.f;
+#pragma unroll
+        for (int kp = 0; kp < (S::KSD + 1) / 2; ++kp) {
+          const int mi = lane >> 3;
+          uint32_t rk[4], rv[4];
+          if (S::KSD - 2 * kp >= 2) {
+            const uint32_t off = swz<S::RBD>(nt * 8 + (lane & 7), 4 * kp + mi);
+            ldsm_x4(k_st + off, rk);
+            ldsm_x4(v_st + off, rv);
+            mma16816<T>(sc[nt], qa[2 * kp], rk);
+            mma16816<T>(sc[nt], qa[2 * kp + 1], rk + 2);
+            mma16816<T>(dp[nt], da[2 * kp], rv);
+            mma16816<T>(dp[nt], da[2 * kp + 1], rv + 2);
+          } else {
+            const uint32_t off = swz<S::RBD>(nt * 8 + (lane & 7), 4 * kp + (mi & 1));
+            ldsm_x2(k_st + off, rk);
+            ldsm_x2(v_st + off, rv);
+            mma16816<T>(sc[nt], qa[2 * kp], rk);
+            mma16816<T>(dp[nt], da[2 * kp], rv);
+          }
+        }
+      }
+      named_sync(rb_bias_full(s), NBAR);
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt) {
+        const uint32_t base = sm + S::OFF_B + s * S::SZ_B + (hl * S::BROW + nt * 16 + 4 * m4) * 4;
+        float4 b0, b1;
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                     : "=f"(b0.x), "=f"(b0.y), "=f"(b0.z), "=f"(b0.w)
+                     : "r"(base + r8 * S::BQ * 4));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
+                     : "=f"(b1.x), "=f"(b1.y), "=f"(b1.z), "=f"(b1.w)
+                     : "r"(base + (r8 + 8) * S::BQ * 4));
+        sc[nt][0] += b0.x;
+        dp[nt][0] += b0.y;
+        sc[nt][1] += b0.z;
+        dp[nt][1] += b0.w;
+        sc[nt][2] += b1.x;
+        dp[nt][2] += b1.y;
+        sc[nt][3] += b1.z;
+        dp[nt][3] += b1.w;
+      }
+      if (n + 2 < nchunks) named_arrive(rb_bias_empty(s), NBAR);
+
+      // P = exp(s - lse), dP' = dP - c; masked keys get P = 0.
+      const bool tail = j0 + S::BN > ev.len;
+      uint32_t pp[4], pd[4];
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int row_hi = i >> 1;
+          float pv = ex2(fmaf(sc[nt][i], kLog2e, -(row_hi ? lse1 : lse0)));
+          if (tail && j0 + nt * 8 + 2 * m4 + (i & 1) >= ev.len) pv = 0.f;
+          sc[nt][i] = pv;
+          dp[nt][i] = pv * (dp[nt][i] - (row_hi ? c1 : c0));
+        }
+      // A fragments (rows on M, keys on K) of [P] and [P dP'].
+      pp[0] = E::pack(sc[0][0], sc[0][1]);
+      pp[1] = E::pack(sc[0][2], sc[0][3]);
+      pp[2] = E::pack(sc[1][0], sc[1][1]);
+      pp[3] = E::pack(sc[1][2], sc[1][3]);
+      pd[0] = E::pack(dp[0][0], dp[0][1]);
+      pd[1] = E::pack(dp[0][2], dp[0][3]);
+      pd[2] = E::pack(dp[1][0], dp[1][1]);
+      pd[3] = E::pack(dp[1][2], dp[1][3]);
+      // Row sums of exactly the rounded values the MMAs consume.
+      psum[0] += (E::lo(pp[0]) + E::hi(pp[0])) + (E::lo(pp[2]) + E::hi(pp[2]));
+      psum[1] += (E::lo(pp[1]) + E::hi(pp[1])) + (E::lo(pp[3]) + E::hi(pp[3]));
+      asum[0] += (E::lo(pd[0]) + E::hi(pd[0])) + (E::lo(pd[2]) + E::hi(pd[2]));
+      asum[1] += (E::lo(pd[1]) + E::hi(pd[1])) + (E::lo(pd[3]) + E::hi(pd[3]));
+
+      if (n >= 2) named_sync(rb_p_empty(s), NBAR);
+      {
+        const uint32_t pb = sm + S::OFF_P + (2 * s) * S::SZ_P + (hl * 8 + m4) * 4;
+        const uint32_t db = sm + S::OFF_P + (2 * s + 1) * S::SZ_P + (hl * 8 + m4) * 4;
+        sts_u32(pb + r8 * S::PQ * 4, pp[0]);
+        sts_u32(pb + r8 * S::PQ * 4 + 16, pp[2]);
+        sts_u32(pb + (r8 + 8) * S::PQ * 4, pp[1]);
+        sts_u32(pb + (r8 + 8) * S::PQ * 4 + 16, pp[3]);
+        sts_u32(db + r8 * S::PQ * 4, pd[0]);
+        sts_u32(db + r8 * S::PQ * 4 + 16, pd[2]);
+        sts_u32(db + (r8 + 8) * S::PQ * 4, pd[1]);
+        sts_u32(db + (r8 + 8) * S::PQ * 4 + 16, pd[3]);
+      }
+      named_arrive(rb_p_full(s), NBAR);
+
+      // X += [P dP'] K, Y += [P] K (B fragments: k = key, n = head dim).
+#pragma unroll
+      for (int np = 0; np < (S::NTD + 1) / 2; ++np) {
+        const int mi = lane >> 3;
+        uint32_t r[4];
+        if (S::NTD - 2 * np >= 2) {
+          ldsm_x4_t(k_st + swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np + (mi >> 1)), r);
+          mma16816<T>(X[2 * np], pd, r);
+          mma16816<T>(X[2 * np + 1], pd, r + 2);
+          mma16816<T>(Y[2 * np], pp, r);
+          mma16816<T>(Y[2 * np + 1], pp, r + 2);
+        } else {
+          ldsm_x2_t(k_st + swz<S::RBD>((mi & 1) * 8 + (lane & 7), 2 * np), r);
+          mma16816<T>(X[2 * np], pd, r);
+          mma16816<T>(Y[2 * np], pp, r);
+        }
+      }
+      __syncwarp();
+      load_kv(n + 2);
+    }
+
+    // D' = a / p, sigma = a - D' p, dqp = X - D' Y (rows r8 and r8 + 8).
+    float dpr[2], sig[2];
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      float av = asum[rh], pv = psum[rh];
+      av += __shfl_xor_sync(0xffffffffu, av, 1);
+      av += __shfl_xor_sync(0xffffffffu, av, 2);
+      pv += __shfl_xor_sync(0xffffffffu, pv, 1);
+      pv += __shfl_xor_sync(0xffffffffu, pv, 2);
+      dpr[rh] = pv > 0.f ? av / pv : 0.f;
+      sig[rh] = av - dpr[rh] * pv;
+      if (m4 == 0) fDp[(r8 + 8 * rh) * S::HP + hl] = dpr[rh];
+    }
+#pragma unroll
+    for (int nd = 0; nd < S::NTD; ++nd) {
+      X[nd][0] -= dpr[0] * Y[nd][0];
+      X[nd][1] -= dpr[0] * Y[nd][1];
+      X[nd][2] -= dpr[1] * Y[nd][2];
+      X[nd][3] -= dpr[1] * Y[nd][3];
+    }
+    __syncthreads();  // (A) D' published
+    __syncthreads();  // (B) E warps published H, G, R
+    const float* fR = (const float*)(smem + S::OFF_R);
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      const int q = r8 + 8 * rh;
+      const bool valid = q < nvalid_q;
+      if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
+      const int64_t row = ev.row0 + q0 + q;
+      T* orow = gdq + vec_off(p, row, h, DH);
+#pragma unroll
+      for (int nd = 0; nd < S::NTD; ++nd) {
+        const int d = nd * 8 + 2 * m4;
+        float v0 = X[nd][2 * rh], v1 = X[nd][2 * rh + 1];
+        if (attn) {
+          v0 += fR[(q * S::HP + hl) * DH + d];
+          v1 += fR[(q * S::HP + hl) * DH + d + 1];
+          if (p.bias) {
+            v0 += sig[rh] * p.bias[d];
+            v1 += sig[rh] * p.bias[d + 1];
+          }
+        }
+        v0 = valid ? v0 * p.scale : 0.f;
+        v1 = valid ? v1 * p.scale : 0.f;
+        *(uint32_t*)(orow + d) = E::pack(v0, v1);
+      }
+      if (m4 == 0) {
+        const int64_t so = stat_off(p, row, h);
+        a.delta[so] = valid ? fCoff[q * S::HP + hl] + dpr[rh] : 0.f;
+        a.sigma[so] = valid ? sig[rh] : 0.f;
+      }
+    }
+  }
+  if (warp >= NH) __syncthreads();  // (B) from the E-warp side
+  __syncthreads();                  // (C) H, G complete for the dW partial
+  // dW partial of this CTA: sum over its valid rows and heads, fixed order.
+  {
+    const float* fH = (const float*)(smem + S::OFF_H);
+    const float* fG = (const float*)(smem + S::OFF_G);
+    for (int o = threadIdx.x; o < DH * C; o += nthreads) {
+      const int d = o / C, c = o - d * C;
+      float acc = 0.f;
+      for (int q = 0; q < nvalid_q; ++q) {
+        const int64_t row = ev.row0 + q0 + q;
+        for (int hl = 0; hl < NH; ++hl) {
+          const int64_t go = vec_off(p, row, h0 + hl, DH) + d;
+          if (attn) acc = fmaf(to_f<T>(gq[go]) * p.scale, fH[(q * S::HP + hl) * C + c], acc);
+          if (act) acc = fmaf(to_f<T>(gdo[go]), fG[(q * S::HP + hl) * C + c], acc);
+        }
+      }
+      dwp[o] = acc;
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+
+template <typename T, int DH, int C>
+static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
+                             int64_t* nparts) {
+  using S = RowShape<DH, C>;
+  const FstProblem& p = a.prob;
+  if constexpr (!S::kFits) {
+    return FST_ERR_UNSUPPORTED;
+  }
+  static bool configured = false;
+  if (!configured) {
+    if (cudaFuncSetAttribute(bwd_rows_tc_kernel<T, DH, C>,
+                             cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
+      return FST_ERR_CUDA;
+    configured = true;
+  }
+  const int groups = (p.heads + S::HP - 1) / S::HP;
+  const int per_group = (p.heads + groups - 1) / groups;
+  const int threads = (per_group + S::NE) * 32;
+  dim3 grid;
+  if (p.packed) {
+    tile_prefix(p, S::BM, tile_start, st);
+    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
+    grid = dim3((unsigned)upper, 1, groups);
+  } else {
+    grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
+  }
+  *nparts = (int64_t)grid.x * grid.y * grid.z;
+  if (grid.x == 0 || grid.y == 0) return FST_OK;
+  bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, 0);
+  count_launch();
+  return FST_OK;
+}
+
+int64_t rows_partials(const FstProblem& p) {
+  constexpr int BM = 16;
+  const int groups = (p.heads + 11) / 12;
+  if (p.packed) return ((p.total_rows + BM - 1) / BM + p.batch) * groups;
+  return (int64_t)((p.max_len + BM - 1) / BM) * p.batch * groups;
+}
+
+template <typename T>
+static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
+  const int D = a.prob.head_dim, C = a.prob.channels;
+  int64_t np = 0;
+#define FST_ROWS_CASE(DD, CC) \
+  if (D == DD && C == CC) return launch_rows_shape<T, DD, CC>(a, st, ts, &np);
+  FST_ROWS_CASE(32, 16)
+  FST_ROWS_CASE(32, 32)
+  FST_ROWS_CASE(32, 64)
+  FST_ROWS_CASE(64, 32)
+  FST_ROWS_CASE(64, 64)
+  FST_ROWS_CASE(16, 16)
+  FST_ROWS_CASE(48, 48)
+#undef FST_ROWS_CASE
+  return FST_ERR_UNSUPPORTED;
+}
+
+int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
+  if (a.prob.dtype == FST_BF16) return launch_rows_t<__nv_bfloat16>(a, st, tile_start);
+  if (a.prob.dtype == FST_F16) return launch_rows_t<__half>(a, st, tile_start);
+  return FST_ERR_UNSUPPORTED;
+}
+
+}  // namespace tc
+}  // namespace fst

@@ -186,22 +186,11 @@ __device__ __forceinline__ float ex2(float x) {
   return r;
 }
 
-// sin and cos of x*f with Cody-Waite argument reduction (W. J. Cody and
-// W. Waite, "Software Manual for the Elementary Functions", 1980): 2*pi is
-// split into C1 + C2 + C3 where C1 carries 8 significant bits, so n*C1 is
-// exact for |n| < 2^16 and x*f - n*C1 is formed by one FMA from the exact
-// product. The reduced argument r in [-pi, pi] goes to the hardware
-// sin.approx / cos.approx, whose absolute error is ~1e-6 on that interval.
-// |x*f| <= 4096 here (x is clipped), so |n| <= 652.
+// sin and cos of x*f: exact-product Cody-Waite reduction to [-pi, pi]
+// (reduce_2pi), then the hardware sin.approx / cos.approx, whose absolute
+// error on that interval is ~1e-6 -- far below the 16-bit rounding of E.
 __device__ __forceinline__ void sincos_xf(float x, float f, float& s, float& c) {
-  const float kInv2Pi = 0.15915494309189535f;
-  const float kC1 = 6.28125f;                 // 2*pi rounded to 12 bits
-  const float kC2 = 1.9353071795864769e-03f;  // next 24 bits of 2*pi
-  const float kC3 = 1.0253377e-11f;           // 2*pi - C1 - C2
-  const float n = rintf(x * f * kInv2Pi);
-  float r = fmaf(x, f, -n * kC1);
-  r = fmaf(-n, kC2, r);
-  r = fmaf(-n, kC3, r);
+  const float r = reduce_2pi(x, f);
   s = __sinf(r);
   c = __cosf(r);
 }

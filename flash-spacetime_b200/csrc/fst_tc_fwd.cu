@@ -724,6 +724,11 @@ __global__ void tile_prefix_kernel(const int32_t* __restrict__ cu, int batch, in
   if (threadIdx.x == 0) tile_start[batch] = carry;
 }
 
+void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st) {
+  tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.batch, bm, tile_start);
+  count_launch();
+}
+
 template <typename T, int DH, int C>
 static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_start,
                             int* status) {
@@ -742,8 +747,7 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
   const int threads = (per_group + S::NE) * 32;
   dim3 grid;
   if (p.packed) {
-    tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.batch, S::BM, tile_start);
-    count_launch();
+    tile_prefix(p, S::BM, tile_start, st);
     const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
     grid = dim3((unsigned)upper, 1, groups);
   } else {

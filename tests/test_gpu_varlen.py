@@ -1,0 +1,176 @@
+"""GPU parity of the packed (varlen) layout: port of upstream tests/test_varlen.py.
+
+1. packed == padded on the same events;
+2. packed forward + backward against the float64 CPU oracle;
+3. bitwise determinism;
+4. uncapped lengths (thousands of pulses) inside a small memory ceiling;
+plus the benchmark's head/channel widths and single-pulse events.
+"""
+
+import pytest
+import torch
+
+import cases as cs
+from oracle import spacetime_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from flash_spacetime.ops import (
+        flash_spacetime_attention,
+        flash_spacetime_attention_varlen,
+    )
+
+LENGTH_MIXES = [
+    [7],
+    [1, 1, 1],
+    [17, 64, 3],
+    [200, 33, 1, 128],
+    [331, 800, 65],
+]
+FLAGS = [(True, True), (True, False), (False, True), (False, False)]
+WIDTHS = [(4, 48, 48), (12, 32, 16)]  # (heads, head_dim, channels)
+
+
+def _to(t, dtype):
+    return t.to(device="cuda", dtype=dtype)
+
+
+def _pad(case, key):
+    lengths = case["lengths"]
+    length = max(lengths)
+    chunks = torch.split(case[key], lengths)
+    if key == "feats":
+        out = case[key].new_zeros(len(lengths), length, case[key].shape[-1])
+        for i, c in enumerate(chunks):
+            out[i, : c.shape[0]] = c
+        return out
+    out = case[key].new_zeros(len(lengths), length, case[key].shape[1], case[key].shape[2])
+    for i, c in enumerate(chunks):
+        out[i, : c.shape[0]] = c
+    return out.permute(0, 2, 1, 3).contiguous()
+
+
+def _unpad(padded, lengths):
+    return torch.cat([padded[i, :, :n].permute(1, 0, 2) for i, n in enumerate(lengths)], 0)
+
+
+@pytest.mark.parametrize("lengths", LENGTH_MIXES)
+@pytest.mark.parametrize("flags", FLAGS)
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("width", WIDTHS)
+def test_varlen_matches_padded(lengths, flags, dtype, width):
+    heads, dim, ch = width
+    case = cs.packed_case(lengths, heads, dim, ch, seed=31 + len(lengths))
+    seqlens = torch.tensor(lengths, device="cuda")
+    w, b = _to(case["weight"], dtype), _to(case["bias"], dtype)
+    out_v = flash_spacetime_attention_varlen(
+        _to(case["q"], dtype), _to(case["k"], dtype), _to(case["v"], dtype),
+        case["feats"].cuda(), w, b, case["cu"].cuda(),
+        use_attn_bias=flags[0], use_activation_bias=flags[1])
+    out_p = flash_spacetime_attention(
+        _to(_pad(case, "q"), dtype), _to(_pad(case, "k"), dtype), _to(_pad(case, "v"), dtype),
+        _pad(case, "feats").cuda(), w, b, seqlens,
+        use_attn_bias=flags[0], use_activation_bias=flags[1])
+    # Same tiles, same arithmetic: the two layouts agree bitwise.
+    assert torch.equal(out_v, _unpad(out_p, lengths))
+
+
+@pytest.mark.parametrize("lengths", LENGTH_MIXES[2:])
+@pytest.mark.parametrize("flags", FLAGS[:2])
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+@pytest.mark.parametrize("width", WIDTHS)
+def test_varlen_matches_oracle(lengths, flags, dtype, width):
+    heads, dim, ch = width
+    case = cs.packed_case(lengths, heads, dim, ch, seed=77 + sum(lengths))
+    leaves = {k: _to(case[k], dtype).requires_grad_(True) for k in ("q", "k", "v", "weight", "bias")}
+    out = flash_spacetime_attention_varlen(
+        leaves["q"], leaves["k"], leaves["v"], case["feats"].cuda(), leaves["weight"],
+        leaves["bias"], case["cu"].cuda(), use_attn_bias=flags[0], use_activation_bias=flags[1])
+    (out.double() * case["grad"].cuda()).sum().backward()
+    ref = orc.oracle_packed(case["q"], case["k"], case["v"], case["feats"], case["weight"],
+                            case["bias"], case["cu"].tolist(), use_attn_bias=flags[0],
+                            use_activation_bias=flags[1], grad_out=case["grad"])
+    names = (("q", "dq"), ("k", "dk"), ("v", "dv"), ("weight", "dW"), ("bias", "db"))
+    if dtype == torch.float32:
+        # upstream tests/test_varlen.py:213-225
+        torch.testing.assert_close(out.detach().double().cpu(), ref["out"], atol=5e-3, rtol=1e-3)
+        for key, rk in names:
+            kg = leaves[key].grad
+            assert kg is not None and ref[rk] is not None
+            torch.testing.assert_close(kg.double().cpu(), ref[rk], atol=5e-2, rtol=5e-3,
+                                       msg=lambda m, key=key: f"grad {key}: {m}")
+        return
+    # 16-bit inputs: upstream's 2x-eager rule against the oracle evaluated in
+    # the same dtype, plus the normwise bound of the port.
+    eager = orc.oracle_packed(case["q"], case["k"], case["v"], case["feats"], case["weight"],
+                              case["bias"], case["cu"].tolist(), use_attn_bias=flags[0],
+                              use_activation_bias=flags[1], grad_out=case["grad"], dtype=dtype)
+    atol = cs.atol_for(dtype, flags)
+    cs.assert_2x_rule(out.detach().cpu().flatten(), eager["out"].flatten(),
+                      ref["out"].flatten(), atol, "forward", dtype)
+    assert cs.normwise(out.detach().cpu(), ref["out"]) <= cs.NORMWISE[dtype]
+    for key, rk in names:
+        kg = leaves[key].grad
+        assert kg is not None and ref[rk] is not None
+        cs.assert_2x_rule(kg.cpu().flatten(), eager[rk].flatten(), ref[rk].flatten(), atol,
+                          f"grad {key}", dtype, reduction=True)
+        if ref[rk].norm() > 1e-8:  # db is analytically zero with the logit term alone
+            assert cs.normwise(kg.cpu(), ref[rk]) <= cs.NORMWISE[dtype], key
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.bfloat16])
+def test_varlen_deterministic(dtype):
+    case = cs.packed_case([64, 17, 200], 16, 48, 48, seed=99)
+    results = []
+    for _ in range(2):
+        q = _to(case["q"], dtype).requires_grad_(True)
+        w = _to(case["weight"], dtype).requires_grad_(True)
+        out = flash_spacetime_attention_varlen(
+            q, _to(case["k"], dtype), _to(case["v"], dtype), case["feats"].cuda(), w,
+            _to(case["bias"], dtype), case["cu"].cuda())
+        out.float().sum().backward()
+        results.append((out.detach().clone(), q.grad.clone(), w.grad.clone()))
+    for a, b in zip(results[0], results[1]):
+        assert torch.equal(a, b)
+
+
+def test_uncapped_lengths_smoke():
+    """Events far beyond any padded cap run within a tight memory budget."""
+    lengths = [6000, 137, 1503]
+    case = cs.packed_case(lengths, 16, 48, 48, seed=7)
+    q = _to(case["q"], torch.bfloat16).requires_grad_(True)
+    w = _to(case["weight"], torch.bfloat16).requires_grad_(True)
+    k, v = _to(case["k"], torch.bfloat16), _to(case["v"], torch.bfloat16)
+    feats, b, cu = case["feats"].cuda(), _to(case["bias"], torch.bfloat16), case["cu"].cuda()
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    base = torch.cuda.memory_allocated()
+    out = flash_spacetime_attention_varlen(q, k, v, feats, w, b, cu)
+    out.float().sum().backward()
+    torch.cuda.synchronize()
+    peak = (torch.cuda.max_memory_allocated() - base) / 2**30
+    assert torch.isfinite(out).all()
+    assert q.grad is not None and torch.isfinite(q.grad).all()
+    assert w.grad is not None and torch.isfinite(w.grad).all()
+    assert peak < 0.5, f"packed fwd+bwd peak {peak:.2f} GiB"
+
+
+def test_single_pulse_events():
+    """Length-1 events attend only to themselves: out = v + R_ii (x = 0, exact).
+
+    The 5-pulse event carries E-dependent outputs, held to upstream's fp32
+    bound for them (tests/test_gpu.py:39-47); the single pulses are exact.
+    """
+    lengths = [1, 1, 5, 1]
+    case = cs.packed_case(lengths, 12, 32, 16, seed=5)
+    out = flash_spacetime_attention_varlen(
+        _to(case["q"], torch.float32), _to(case["k"], torch.float32),
+        _to(case["v"], torch.float32), case["feats"].cuda(), _to(case["weight"], torch.float32),
+        _to(case["bias"], torch.float32), case["cu"].cuda())
+    ref = orc.oracle_packed(case["q"], case["k"], case["v"], case["feats"], case["weight"],
+                            case["bias"], case["cu"].tolist())
+    out = out.double().cpu()
+    single = torch.tensor([0, 1, 7])  # rows of the length-1 events
+    torch.testing.assert_close(out[single], ref["out"][single], atol=1e-6, rtol=1e-6)
+    torch.testing.assert_close(out, ref["out"], atol=5e-3, rtol=1e-3)

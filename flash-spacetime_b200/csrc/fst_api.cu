@@ -97,7 +97,6 @@ int fst_forward(const FstForwardArgs* a, void* stream) {
   if (p.total_rows > 0) {
     if (!a->q || !a->k || !a->v || !a->out || !a->lse)
       return fail(FST_ERR_INVALID, "forward: q, k, v, out and lse are required");
-    if (p.use_attn_bias && !a->u) return fail(FST_ERR_INVALID, "forward: u required (attn bias)");
   }
   const size_t need = fst_forward_workspace_size(&p);
   if (need > 0 && (!a->workspace || a->workspace_bytes < need))
@@ -119,13 +118,12 @@ int fst_backward(const FstBackwardArgs* a, void* stream) {
   int rc = check_problem(&a->prob);
   if (rc) return rc;
   const FstProblem& p = a->prob;
-  if (!a->dw_partial) return fail(FST_ERR_INVALID, "backward: dw_partial is required");
+  if (!a->dw_partial || !a->db_partial)
+    return fail(FST_ERR_INVALID, "backward: dw_partial and db_partial are required");
   if (p.total_rows > 0) {
     if (!a->q || !a->k || !a->v || !a->dout || !a->lse || !a->dq || !a->dk || !a->dv ||
         !a->delta || !a->sigma)
       return fail(FST_ERR_INVALID, "backward: a required pointer is null");
-    if (p.use_attn_bias && !a->u) return fail(FST_ERR_INVALID, "backward: u required");
-    if (p.use_act_bias && !a->wt) return fail(FST_ERR_INVALID, "backward: wt required");
   }
   const size_t need = fst_backward_workspace_size(&p);
   if (need > 0 && (!a->workspace || a->workspace_bytes < need))

@@ -75,6 +75,12 @@ __device__ __forceinline__ int64_t vec_off(const FstProblem& p, int64_t row, int
   return ((b * p.heads + h) * p.max_len + i) * (int64_t)dim;
 }
 
+// Element stride between consecutive rows of one event for a fixed head:
+// packed [T, H, D] rows are H*D apart, padded [B, H, L, D] rows D apart.
+__device__ __forceinline__ int row_stride(const FstProblem& p, int dim) {
+  return p.packed ? p.heads * dim : dim;
+}
+
 // Offset of (row, head) in a per-row-per-head fp32 vector (LSE, D, sigma).
 __device__ __forceinline__ int64_t stat_off(const FstProblem& p, int64_t row, int h) {
   return vec_off(p, row, h, 1);

@@ -63,6 +63,17 @@ __device__ __forceinline__ void embed(float x, const float* freqs, int C, float*
   }
 }
 
+// sum_d x[d] W[d][c] in fp32, rounded to T as the host-side projection is.
+template <typename T>
+__device__ __forceinline__ float project(const FstProblem& p, const float* x, int c, int D, int C,
+                                         T) {
+  float acc = 0.f;
+#pragma unroll
+  for (int d = 0; d < kMax; ++d)
+    if (d < D) acc = fmaf(x[d], p.weight[(int64_t)d * C + c], acc);
+  return to_f<T>(from_f<T>(acc));
+}
+
 template <typename T>
 __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
   const FstProblem& p = a.prob;
@@ -90,7 +101,9 @@ __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
   const int64_t uoff = vec_off(p, t.row, t.h, C);
 #pragma unroll
   for (int c = 0; c < kMax; ++c) {
-    uu[c] = (p.use_attn_bias && c < C) ? to_f<T>(u[uoff + c]) : 0.f;
+    uu[c] = (p.use_attn_bias && c < C)
+                ? (u ? to_f<T>(u[uoff + c]) : project(p, qt, c, D, C, from_f<T>(0.f)))
+                : 0.f;
     ae[c] = 0.f;
     e[c] = 0.f;
   }
@@ -175,8 +188,12 @@ __device__ __forceinline__ void load_bwd_row(const FstBackwardArgs& a, int64_t r
   }
 #pragma unroll
   for (int c = 0; c < kMax; ++c) {
-    r.uu[c] = (p.use_attn_bias && c < C) ? to_f<T>(((const T*)a.u)[coff + c]) : 0.f;
-    r.wt[c] = (p.use_act_bias && c < C) ? to_f<T>(((const T*)a.wt)[coff + c]) : 0.f;
+    r.uu[c] = 0.f;
+    r.wt[c] = 0.f;
+    if (c < C && p.use_attn_bias)
+      r.uu[c] = a.u ? to_f<T>(((const T*)a.u)[coff + c]) : project(p, r.qt, c, D, C, T());
+    if (c < C && p.use_act_bias)
+      r.wt[c] = a.wt ? to_f<T>(((const T*)a.wt)[coff + c]) : project(p, r.dov, c, D, C, T());
   }
   r.off = c;
   r.lse = a.lse[stat_off(p, row, h)];
@@ -380,6 +397,19 @@ __global__ void __launch_bounds__(256) dw_partial_kernel(FstBackwardArgs a, cons
       if (p.use_act_bias) acc = fmaf(to_f<T>(dout[off + d]), gbuf[coff + c], acc);
     }
     a.dw_partial[(int64_t)blockIdx.x * D * C + o] = acc;
+  }
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int64_t g = r0; g < r1; ++g) {
+      const int64_t row = g / p.heads;
+      const int h = (int)(g - row * p.heads);
+      if (!p.packed) {
+        const int64_t b = row / p.max_len;
+        if (row - b * p.max_len >= p.seqlens[b]) continue;
+      }
+      acc += to_f<T>(dout[vec_off(p, row, h, D) + d]);
+    }
+    a.db_partial[(int64_t)blockIdx.x * D + d] = acc;
   }
 }
 

@@ -45,10 +45,13 @@ struct ColShape {
   static constexpr int DHP = DH <= 16 ? 16 : (DH <= 32 ? 32 : 64);
   static constexpr int CP = C <= 16 ? 16 : (C <= 32 ? 32 : 64);
   static constexpr int RBD = DHP * 2, RBC = CP * 2;
-  // bias tile [head][key][query] of (u.E, w~.E) pairs: 32 words per key row
-  // + 16 pad so two key rows of a 16-byte load wavefront use distinct banks.
-  static constexpr int JS = 48;
-  static constexpr int HS = BK * JS;
+  // bias tile [head][key][query] of (u.E, w~.E) pairs: 32 words per key row,
+  // 8 pad words per head, and the 16-byte chunk of a query pair XOR-swizzled
+  // by the key (bias_chunk) -- a layout searched so that the E-warp stores
+  // are at most 2-way bank conflicted and the head-warp 16-byte loads are
+  // conflict free.
+  static constexpr int JS = 32;
+  static constexpr int HS = BK * JS + 8;
   static constexpr int SZ_BIAS = HP * HS * 4;                 // one stage
   // head-warp ring stage: Q chunk, dO chunk [BQ][DHP] + lse2, delta [BQ]
   static constexpr int SZ_HR = 2 * BQ * RBD + 2 * BQ * 4;
@@ -69,13 +72,20 @@ struct ColShape {
   static constexpr bool kFits = SMEM <= 227 * 1024;
 };
 
+// Word offset of the (u, w) pair of (key j, query q) inside one head's tile.
+__device__ __forceinline__ int bias_word(int j, int q, int js) {
+  const int g = ((j >> 1) & 3) | ((j & 1) << 2);
+  return j * js + 4 * ((q >> 1) ^ g) + 2 * (q & 1);
+}
+
 __device__ __forceinline__ int cb_bias_full(int s) { return 1 + s; }
 __device__ __forceinline__ int cb_bias_empty(int s) { return 3 + s; }
 
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     bwd_cols_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
-                       int heads_per_group) {
+                       int heads_per_group, const T* __restrict__ gu,
+                       const T* __restrict__ gwt) {
   using S = ColShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -171,11 +181,14 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   if (warp >= NH) {
     // =============================== E warps ==============================
     const int e = warp - NH;
-    float fr[S::FG][2];
+    float fr[S::FG][2], fv[S::FG][2];  // f and f / (2 pi) of this lane's frequencies
 #pragma unroll
     for (int g = 0; g < S::FG; ++g) {
-      fr[g][0] = p.freqs[8 * g + 2 * m4];
-      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        fr[g][r] = p.freqs[8 * g + 2 * m4 + r];
+        fv[g][r] = fr[g][r] * 0.15915494309189535f;
+      }
     }
     // Coordinates of the two keys this lane pairs with (n-tile 0 and 1).
     Coord4 ck[2];
@@ -188,6 +201,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       ck[nt].t = fKC[j * 4 + 3];
     }
     const uint32_t ring = sm + S::OFF_ER + e * 2 * S::SZ_ER;
+    const int rsc = row_stride(p, C);
+    const float* __restrict__ fbase = p.feats + ev.row0 * p.feat_stride;
     auto load_ring = [&](int n) {
       if (n < nchunks) {
         const uint32_t st = ring + (n & 1) * S::SZ_ER;
@@ -197,9 +212,9 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
           const int i = n * S::BQ + e * S::QPE + t;
           const uint32_t off = swz<S::RBC>(t * S::HP + h, c);
           if (i < ev.len) {
-            const int64_t go = vec_off(p, ev.row0 + i, h0 + h, C) + c * 8;
-            if (attn) cp_async16(st + off, (const T*)a.u + go);
-            if (act) cp_async16(st + S::UW + off, (const T*)a.wt + go);
+            const int64_t go = vec_off(p, ev.row0, h0 + h, C) + (int64_t)i * rsc + c * 8;
+            if (attn) cp_async16(st + off, gu + go);
+            if (act) cp_async16(st + S::UW + off, gwt + go);
           } else {
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + off), "r"(0));
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + S::UW + off),
@@ -210,7 +225,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
           const int i = n * S::BQ + e * S::QPE + lane;
           const uint32_t dst = st + 2 * S::UW + lane * 16;
           if (i < ev.len)
-            cp_async16(dst, p.feats + (ev.row0 + i) * p.feat_stride);
+            cp_async16(dst, fbase + i * p.feat_stride);
           else
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
         }
@@ -251,8 +266,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
         cq.y = c4.y;
         cq.z = c4.z;
         cq.t = c4.w;
-        xl[0] = pair_angle(cq, ck[0]);
-        xl[1] = pair_angle(cq, ck[1]);
+        xl[0] = pair_angle_fast(cq, ck[0]);
+        xl[1] = pair_angle_fast(cq, ck[1]);
       }
       __syncwarp();
       load_ring(n + 2);
@@ -267,7 +282,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
         }
         const int qq = e * S::QPE + t;  // query index within the chunk
 #pragma unroll
@@ -290,12 +305,13 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
             if (act) mma16816<T>(dw, wa[t][ks], eb[ks]);
           }
           // D[h][key]: h = r8 (+8), keys nt*8 + 2 m4 (+1). Tile [h][key][q].
-          const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS + (2 * qq) * 4;
+          const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS;
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
             const int j = nt * 8 + 2 * m4 + r;
-            if (r8 < NH) sts_v2(base + (r8 * S::HS + j * S::JS) * 4, du[r], dw[r]);
-            if (r8 + 8 < NH) sts_v2(base + ((r8 + 8) * S::HS + j * S::JS) * 4, du[2 + r], dw[2 + r]);
+            const int w = bias_word(j, qq, S::JS);
+            if (r8 < NH) sts_v2(base + (r8 * S::HS + w) * 4, du[r], dw[r]);
+            if (r8 + 8 < NH) sts_v2(base + ((r8 + 8) * S::HS + w) * 4, du[2 + r], dw[2 + r]);
           }
         }
       }
@@ -308,6 +324,9 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   const int hl = warp;
   const int h = h0 + hl;
   const uint32_t ring = sm + S::OFF_HR + hl * 2 * S::SZ_HR;
+  const T* __restrict__ qbase = gq + vec_off(p, ev.row0, h, DH);
+  const T* __restrict__ dobase = gdo + vec_off(p, ev.row0, h, DH);
+  const int rs = row_stride(p, DH);
   auto load_ring = [&](int n) {
     if (n < nchunks) {
       const uint32_t st = ring + (n & 1) * S::SZ_HR;
@@ -317,9 +336,9 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
         const uint32_t off = swz<S::RBD>(i, c);
         const int qi = n * S::BQ + i;
         if (qi < ev.len) {
-          const int64_t go = vec_off(p, ev.row0 + qi, h, DH) + c * 8;
-          cp_async16(st + off, gq + go);
-          cp_async16(st + S::BQ * S::RBD + off, gdo + go);
+          const int go = qi * rs + c * 8;
+          cp_async16(st + off, qbase + go);
+          cp_async16(st + S::BQ * S::RBD + off, dobase + go);
         } else {
           asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + off), "r"(0));
           asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(st + S::BQ * S::RBD + off),
@@ -404,15 +423,15 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
       // keys r8 (+8), queries nt*8 + 2 m4 (+1): (u, w) pairs, 16 bytes per key.
-      const uint32_t base =
-          sm + S::OFF_BIAS + s * S::SZ_BIAS + (hl * S::HS + 2 * (nt * 8 + 2 * m4)) * 4;
+      const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS + hl * S::HS * 4;
+      const int q = nt * 8 + 2 * m4;
       float4 b0, b1;
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
                    : "=f"(b0.x), "=f"(b0.y), "=f"(b0.z), "=f"(b0.w)
-                   : "r"(base + r8 * S::JS * 4));
+                   : "r"(base + bias_word(r8, q, S::JS) * 4));
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
                    : "=f"(b1.x), "=f"(b1.y), "=f"(b1.z), "=f"(b1.w)
-                   : "r"(base + (r8 + 8) * S::JS * 4));
+                   : "r"(base + bias_word(r8 + 8, q, S::JS) * 4));
       sc[nt][0] += b0.x;
       dp[nt][0] += b0.y;
       sc[nt][1] += b0.z;
@@ -427,18 +446,25 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     // P^T and dS^T; queries past the event (last chunk) get P = 0.
     uint32_t pt[4], dt[4];
     float amax[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [nt][column pair member]
+    const bool qtail = i0 + S::BQ > ev.len;  // queries past the event: last chunk only
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int qi = nt * 8 + 2 * m4 + (i & 1);
-        float pv = ex2(fmaf(sc[nt][i], kLog2e, -stat[qi]));
-        if (i0 + qi >= ev.len) pv = 0.f;
-        const float ds = pv * (dp[nt][i] - stat[S::BQ + qi]);
-        sc[nt][i] = pv;
-        dp[nt][i] = ds;
-        if ((i >> 1) == 0 ? (r8 < nvalid_k) : (r8 + 8 < nvalid_k))
-          amax[nt][i & 1] = fmaxf(amax[nt][i & 1], fabsf(ds));
+      for (int c = 0; c < 2; ++c) {
+        const int qi = nt * 8 + 2 * m4 + c;
+        const float l2 = stat[qi], dl = stat[S::BQ + qi];
+        const bool dead = qtail && i0 + qi >= ev.len;
+#pragma unroll
+        for (int hi = 0; hi < 2; ++hi) {
+          const int i = 2 * hi + c;
+          float pv = ex2(fmaf(sc[nt][i], kLog2e, -l2));
+          if (dead) pv = 0.f;
+          const float ds = pv * (dp[nt][i] - dl);
+          sc[nt][i] = pv;
+          dp[nt][i] = ds;
+          if (hi == 0 ? (r8 < nvalid_k) : (r8 + 8 < nvalid_k))
+            amax[nt][c] = fmaxf(amax[nt][c], fabsf(ds));
+        }
       }
     pt[0] = E::pack(sc[0][0], sc[0][1]);
     pt[1] = E::pack(sc[0][2], sc[0][3]);
@@ -509,7 +535,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 // ---------------------------------------------------------------------------
 
 template <typename T, int DH, int C>
-static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
+static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
+                             const void* gu, const void* gwt) {
   using S = ColShape<DH, C>;
   const FstProblem& p = a.prob;
   if constexpr (!S::kFits) {
@@ -535,17 +562,19 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
       grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
     }
     if (grid.x == 0 || grid.y == 0) return FST_OK;
-    bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group);
+    bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
+                                                                 (const T*)gu, (const T*)gwt);
     count_launch();
     return FST_OK;
   }
 }
 
 template <typename T>
-static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
+static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, const void* gu,
+                         const void* gwt) {
   const int D = a.prob.head_dim, C = a.prob.channels;
 #define FST_COLS_CASE(DD, CC) \
-  if (D == DD && C == CC) return launch_cols_shape<T, DD, CC>(a, st, ts);
+  if (D == DD && C == CC) return launch_cols_shape<T, DD, CC>(a, st, ts, gu, gwt);
   FST_COLS_CASE(32, 16)
   FST_COLS_CASE(32, 32)
   FST_COLS_CASE(32, 64)
@@ -557,9 +586,10 @@ static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
   return FST_ERR_UNSUPPORTED;
 }
 
-int launch_bwd_cols(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
-  if (a.prob.dtype == FST_BF16) return launch_cols_t<__nv_bfloat16>(a, st, tile_start);
-  if (a.prob.dtype == FST_F16) return launch_cols_t<__half>(a, st, tile_start);
+int launch_bwd_cols(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, const void* gu,
+                    const void* gwt) {
+  if (a.prob.dtype == FST_BF16) return launch_cols_t<__nv_bfloat16>(a, st, tile_start, gu, gwt);
+  if (a.prob.dtype == FST_F16) return launch_cols_t<__half>(a, st, tile_start, gu, gwt);
   return FST_ERR_UNSUPPORTED;
 }
 
@@ -567,19 +597,34 @@ bool bwd_supported(const FstProblem& p) {
   return fwd_supported(p);  // same (Dh, C) list; every shape fits both kernels
 }
 
+// Workspace: [status 64 B][tile prefix, B+1 ints][u and w~, rows x H x C each
+// in the 16-bit type, 256-byte aligned] -- the row kernel writes the two
+// projections there when the caller did not pass them, the column kernel
+// reads them back.
+static size_t ws_proj_offset(const FstProblem& p) {
+  return (64 + (size_t)(p.batch + 1) * sizeof(int) + 255) / 256 * 256;
+}
+static size_t ws_proj_bytes(const FstProblem& p) {
+  return ((size_t)p.total_rows * p.heads * p.channels * 2 + 255) / 256 * 256;
+}
+
 size_t bwd_workspace(const FstProblem& p) {
-  return (size_t)(p.batch + 1) * sizeof(int) + 64;
+  return ws_proj_offset(p) + 2 * ws_proj_bytes(p);
 }
 
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st) {
+  const FstProblem& p = a.prob;
   int* tile_start = (int*)a.workspace + 16;
+  unsigned char* proj = (unsigned char*)a.workspace + ws_proj_offset(p);
+  void* u_ws = proj;
+  void* wt_ws = proj + ws_proj_bytes(p);
   if (a.ds_absmax) {
-    const int64_t n = a.prob.total_rows * a.prob.heads;
+    const int64_t n = p.total_rows * p.heads;
     if (cudaMemsetAsync(a.ds_absmax, 0, n * sizeof(float), st) != cudaSuccess) return FST_ERR_CUDA;
   }
-  int rc = launch_bwd_rows(a, st, tile_start);
+  int rc = launch_bwd_rows(a, st, tile_start, u_ws, wt_ws);
   if (rc) return rc;
-  return launch_bwd_cols(a, st, tile_start);
+  return launch_bwd_cols(a, st, tile_start, a.u ? a.u : u_ws, a.wt ? a.wt : wt_ws);
 }
 
 }  // namespace tc

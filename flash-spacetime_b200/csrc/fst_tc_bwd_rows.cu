@@ -92,7 +92,7 @@ __device__ __forceinline__ int rb_p_empty(int s) { return 7 + s; }
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     bwd_rows_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
-                       int heads_per_group, int n_row_tiles) {
+                       int heads_per_group, T* __restrict__ u_ws, T* __restrict__ wt_ws) {
   using S = RowShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -109,6 +109,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const int64_t part = (int64_t)blockIdx.z * gridDim.x + blockIdx.x;
       for (int i = threadIdx.x; i < DH * C; i += blockDim.x)
         a.dw_partial[part * DH * C + i] = 0.f;
+      for (int i = threadIdx.x; i < DH; i += blockDim.x) a.db_partial[part * DH + i] = 0.f;
       return;
     }
     int lo = 0, hi = p.batch - 1;
@@ -123,6 +124,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
                                 : (((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x +
                                    blockIdx.x);
   float* dwp = a.dw_partial + part * DH * C;
+  float* dbp = a.db_partial + part * DH;
   const EventSpan ev = event_span(p, b);
   const int q0 = qb * S::BM;
   const int h0 = blockIdx.z * heads_per_group;
@@ -140,6 +142,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
   if (q0 >= ev.len) {
     for (int i = threadIdx.x; i < DH * C; i += nthreads) dwp[i] = 0.f;
+    for (int i = threadIdx.x; i < DH; i += nthreads) dbp[i] = 0.f;
     if (!p.packed) {
       for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
         const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
@@ -169,20 +172,28 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
       uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
-      if (q < nvalid_q) {
+      if (q < nvalid_q) {  // raw q (scaled in place after the projections)
         const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8;
-        const uint4 raw = *(const uint4*)(gq + go);
+        vq = *(const uint4*)(gq + go);
         vd = *(const uint4*)(gdo + go);
-        const uint32_t* w = (const uint32_t*)&raw;
-        uint32_t* o = (uint32_t*)&vq;
-#pragma unroll
-        for (int i = 0; i < 4; ++i) o[i] = E::pack(E::lo(w[i]) * p.scale, E::hi(w[i]) * p.scale);
       }
       const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
       *(uint4*)(smem + S::OFF_Q + off) = vq;
       *(uint4*)(smem + S::OFF_DO + off) = vd;
     }
   }
+  __syncthreads();
+  // u = (q * scale) W and w~ = dO W in fp32 from the staged raw rows, unless
+  // the caller passed them; they go to the workspace, where phase 2 below and
+  // the column kernel read them.
+  if (attn && a.u == nullptr)
+    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev.row0 + q0,
+                                            nvalid_q, S::BM, h0, NH, nullptr, u_ws);
+  if (act && a.wt == nullptr)
+    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_DO, S::BM, 1.f, ev.row0 + q0,
+                                            nvalid_q, S::BM, h0, NH, nullptr, wt_ws);
+  __syncthreads();
+  scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();
   const int m4 = lane & 3, r8 = lane >> 2;
   const bool idle = warp >= NH + NE;
@@ -200,19 +211,12 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   }
   __syncthreads();  // phase 2 of the staging reuses the Q / dO bytes
   {
-    constexpr int UCH = S::CP / 8;
-    for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
-      const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
-      uint4 vu = make_uint4(0, 0, 0, 0), vw = make_uint4(0, 0, 0, 0);
-      if (q < nvalid_q && h < NH && c * 8 < C) {
-        const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8;
-        if (attn) vu = *(const uint4*)((const T*)a.u + go);
-        if (act) vw = *(const uint4*)((const T*)a.wt + go);
-      }
-      const uint32_t off = swz<S::RBC>(q * 16 + h, c);
-      *(uint4*)(smem + S::OFF_U + off) = vu;
-      *(uint4*)(smem + S::OFF_WT + off) = vw;
-    }
+    if (attn)
+      stage_rows<T, C, S::CP>(p, a.u ? (const T*)a.u : u_ws, ev.row0 + q0, nvalid_q, S::BM, h0,
+                              NH, smem + S::OFF_U);
+    if (act)
+      stage_rows<T, C, S::CP>(p, a.wt ? (const T*)a.wt : wt_ws, ev.row0 + q0, nvalid_q, S::BM,
+                              h0, NH, smem + S::OFF_WT);
     for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
       const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
       float w0 = 0.f, w1 = 0.f;
@@ -280,11 +284,14 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     // =============================== E warps ==============================
     const int e = warp - NH;
     const int qe = e * S::QPE;
-    float fr[S::FG][2];
+    float fr[S::FG][2], fv[S::FG][2];  // f and f / (2 pi) of this lane's frequencies
 #pragma unroll
     for (int g = 0; g < S::FG; ++g) {
-      fr[g][0] = p.freqs[8 * g + 2 * m4];
-      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        fr[g][r] = p.freqs[8 * g + 2 * m4 + r];
+        fv[g][r] = fr[g][r] * 0.15915494309189535f;
+      }
     }
     const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
     Coord4 cq;
@@ -293,12 +300,13 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     cq.z = fQC[qx_row * 4 + 2];
     cq.t = fQC[qx_row * 4 + 3];
     const uint32_t c_ring = sm + S::OFF_C + e * 2 * S::BN * 16;
+    const float* __restrict__ fbase = p.feats + ev.row0 * p.feat_stride;
     auto load_coords = [&](int n) {
       if (n < nchunks && lane < S::BN) {
         const int j = n * S::BN + lane;
         const uint32_t dst = c_ring + ((n & 1) * S::BN + lane) * 16;
         if (j < ev.len)
-          cp_async16(dst, p.feats + (ev.row0 + j) * p.feat_stride);
+          cp_async16(dst, fbase + j * p.feat_stride);
         else
           asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
       }
@@ -329,7 +337,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         c4.y = ck.y;
         c4.z = ck.z;
         c4.t = ck.w;
-        xl[nt] = pair_angle(cq, c4);
+        xl[nt] = pair_angle_fast(cq, c4);
       }
       __syncwarp();
       load_coords(n + 2);
@@ -345,7 +353,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
         }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)
@@ -482,6 +490,11 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     const int h = h0 + hl;
     const uint32_t k_ring = sm + S::OFF_K + hl * S::BN * S::RBD;
     const uint32_t v_ring = sm + S::OFF_V + hl * S::BN * S::RBD;
+    // K / V of this head: event base pointer and row stride (no 64-bit math
+    // per copy).
+    const T* __restrict__ kbase = gk + vec_off(p, ev.row0, h, DH);
+    const T* __restrict__ vbase = gv + vec_off(p, ev.row0, h, DH);
+    const int rs = row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
         constexpr int CH = DH / 8;
@@ -491,9 +504,9 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
           const int c = idx % CH, j = idx / CH;
           const uint32_t off = swz<S::RBD>(j, c);
           if (j0 + j < ev.len) {
-            const int64_t go = vec_off(p, ev.row0 + j0 + j, h, DH) + c * 8;
-            cp_async16(ks_ + off, gk + go);
-            cp_async16(vs_ + off, gv + go);
+            const int go = (j0 + j) * rs + c * 8;
+            cp_async16(ks_ + off, kbase + go);
+            cp_async16(vs_ + off, vbase + go);
           } else {
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(ks_ + off), "r"(0));
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(vs_ + off), "r"(0));
@@ -569,18 +582,23 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       if (n + 2 < nchunks) named_arrive(rb_bias_empty(s), NBAR);
 
       // P = exp(s - lse), dP' = dP - c; masked keys get P = 0.
-      const bool tail = j0 + S::BN > ev.len;
       uint32_t pp[4], pd[4];
 #pragma unroll
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const int row_hi = i >> 1;
-          float pv = ex2(fmaf(sc[nt][i], kLog2e, -(row_hi ? lse1 : lse0)));
-          if (tail && j0 + nt * 8 + 2 * m4 + (i & 1) >= ev.len) pv = 0.f;
-          sc[nt][i] = pv;
-          dp[nt][i] = pv * (dp[nt][i] - (row_hi ? c1 : c0));
-        }
+        for (int i = 0; i < 4; ++i) sc[nt][i] = ex2(fmaf(sc[nt][i], kLog2e, (i >> 1) ? -lse1 : -lse0));
+      if (j0 + S::BN > ev.len) {  // keys past the event: last chunk only
+        const int lim = ev.len - j0 - 2 * m4;
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+          for (int i = 0; i < 4; ++i)
+            if (nt * 8 + (i & 1) >= lim) sc[nt][i] = 0.f;
+      }
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i) dp[nt][i] = sc[nt][i] * (dp[nt][i] - ((i >> 1) ? c1 : c0));
       // A fragments (rows on M, keys on K) of [P] and [P dP'].
       pp[0] = E::pack(sc[0][0], sc[0][1]);
       pp[1] = E::pack(sc[0][2], sc[0][3]);
@@ -704,6 +722,14 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       }
       dwp[o] = acc;
     }
+    // db partial: sum of dO over the valid rows and heads (backward.py:615-622).
+    for (int d = threadIdx.x; d < DH; d += nthreads) {
+      float acc = 0.f;
+      for (int q = 0; q < nvalid_q; ++q)
+        for (int hl = 0; hl < NH; ++hl)
+          acc += to_f<T>(gdo[vec_off(p, ev.row0 + q0 + q, h0 + hl, DH) + d]);
+      dbp[d] = acc;
+    }
   }
 }
 
@@ -711,7 +737,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
 template <typename T, int DH, int C>
 static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
-                             int64_t* nparts) {
+                             void* u_ws, void* wt_ws, int64_t* nparts) {
   using S = RowShape<DH, C>;
   const FstProblem& p = a.prob;
   if constexpr (!S::kFits) {
@@ -737,7 +763,8 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   }
   *nparts = (int64_t)grid.x * grid.y * grid.z;
   if (grid.x == 0 || grid.y == 0) return FST_OK;
-  bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, 0);
+  bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
+                                                                 (T*)u_ws, (T*)wt_ws);
   count_launch();
   return FST_OK;
 }
@@ -750,11 +777,12 @@ int64_t rows_partials(const FstProblem& p) {
 }
 
 template <typename T>
-static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
+static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, void* u_ws,
+                         void* wt_ws) {
   const int D = a.prob.head_dim, C = a.prob.channels;
   int64_t np = 0;
 #define FST_ROWS_CASE(DD, CC) \
-  if (D == DD && C == CC) return launch_rows_shape<T, DD, CC>(a, st, ts, &np);
+  if (D == DD && C == CC) return launch_rows_shape<T, DD, CC>(a, st, ts, u_ws, wt_ws, &np);
   FST_ROWS_CASE(32, 16)
   FST_ROWS_CASE(32, 32)
   FST_ROWS_CASE(32, 64)
@@ -766,9 +794,11 @@ static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts) {
   return FST_ERR_UNSUPPORTED;
 }
 
-int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start) {
-  if (a.prob.dtype == FST_BF16) return launch_rows_t<__nv_bfloat16>(a, st, tile_start);
-  if (a.prob.dtype == FST_F16) return launch_rows_t<__half>(a, st, tile_start);
+int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, void* u_ws,
+                    void* wt_ws) {
+  if (a.prob.dtype == FST_BF16)
+    return launch_rows_t<__nv_bfloat16>(a, st, tile_start, u_ws, wt_ws);
+  if (a.prob.dtype == FST_F16) return launch_rows_t<__half>(a, st, tile_start, u_ws, wt_ws);
   return FST_ERR_UNSUPPORTED;
 }
 

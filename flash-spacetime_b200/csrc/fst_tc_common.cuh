@@ -186,13 +186,143 @@ __device__ __forceinline__ float ex2(float x) {
   return r;
 }
 
-// sin and cos of x*f: exact-product Cody-Waite reduction to [-pi, pi]
-// (reduce_2pi), then the hardware sin.approx / cos.approx, whose absolute
-// error on that interval is ~1e-6 -- far below the 16-bit rounding of E.
-__device__ __forceinline__ void sincos_xf(float x, float f, float& s, float& c) {
-  const float r = reduce_2pi(x, f);
+// sin and cos of x*f for the 16-bit kernels. Exact-product Cody-Waite
+// reduction to [-pi, pi] (as reduce_2pi, with the third constant dropped: its
+// contribution is < 1e-8 rad for |n| <= 652), the nearest integer n formed on
+// the FMA pipe by the 1.5*2^23 rounding constant instead of rintf, and the
+// hardware sin.approx / cos.approx (absolute error ~1e-6 on [-pi, pi], far
+// below the 16-bit rounding of E). f_rev = f / (2 pi) is precomputed.
+__device__ __forceinline__ void sincos_xf(float x, float f, float f_rev, float& s, float& c) {
+  const float kRound = 12582912.f;            // 1.5 * 2^23
+  const float kC1 = 6.28125f;
+  const float kC2 = 1.9353071795864769e-03f;
+  const float n = fmaf(x, f_rev, kRound) - kRound;
+  float r = fmaf(x, f, -n * kC1);
+  r = fmaf(-n, kC2, r);
   s = __sinf(r);
   c = __cosf(r);
+}
+
+// x_ij for the 16-bit kernels: as pair_angle, with the square root taken by
+// sqrt.approx (one MUFU op) and the clip applied before it -- |I| >= 16 maps
+// straight to +-4096, the exact value the clipped branch takes.
+__device__ __forceinline__ float pair_angle_fast(const Coord4& a, const Coord4& b) {
+  const float dx = a.x - b.x, dy = a.y - b.y, dz = a.z - b.z;
+  const float dt = (a.t - b.t) * kTimeScale;
+  const float iv = dx * dx + dy * dy + dz * dz - dt * dt;
+  const float m = fabsf(iv);
+  float r;
+  asm("sqrt.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(m));
+  const float x = m >= 16.f ? 4096.f : kInputScale * r;
+  return copysignf(x, iv);
+}
+
+// Projection of a block of rows through the encoder weight, in fp32:
+//   out[q][h][c] = [ sum_d (x[q, h0+h, d] * mul) W[d][c] ]   (x: [rows, H, DH] in T)
+// rounded once to T -- the same arithmetic as the host-side
+// ((x.float() * mul) @ W).to(dtype) of upstream forward.py:279-286 and
+// backward.py:546-547, up to the order of the DH-term sum. The result goes
+// to a swizzled shared tile [q][16][CP] (head rows >= NH, channels >= C and
+// rows >= nvalid are written as zeros) and, if gdst is given, to global
+// memory in the [rows, H, C] layout of x.
+template <typename T, int DH, int C, int CP>
+__device__ __forceinline__ void project_rows(const FstProblem& p, const T* __restrict__ x,
+                                             float mul, int64_t row0, int nvalid, int nrows,
+                                             int h0, int NH, unsigned char* tile,
+                                             T* __restrict__ gdst) {
+  using E = Elem<T>;
+  constexpr int RBC = CP * 2;
+  for (int idx = threadIdx.x; idx < nrows * 16 * (CP / 2); idx += blockDim.x) {
+    const int c2 = idx % (CP / 2), h = (idx / (CP / 2)) % 16, q = idx / (16 * (CP / 2));
+    uint32_t packed = 0u;
+    if (q < nvalid && h < NH && 2 * c2 < C) {
+      const int64_t row = row0 + q;
+      const T* xr = x + vec_off(p, row, h0 + h, DH);
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll 8
+      for (int d = 0; d < DH; ++d) {
+        const float xv = to_f<T>(xr[d]) * mul;
+        const float2 w = *(const float2*)(p.weight + (int64_t)d * C + 2 * c2);
+        a0 = fmaf(xv, w.x, a0);
+        a1 = fmaf(xv, w.y, a1);
+      }
+      packed = E::pack(a0, a1);
+      if (gdst) *(uint32_t*)(gdst + vec_off(p, row, h0 + h, C) + 2 * c2) = packed;
+    }
+    *(uint32_t*)(tile + swz<RBC>(q * 16 + h, c2 / 4) + (c2 % 4) * 4) = packed;
+  }
+}
+
+// As project_rows, reading x from a staged shared tile [h][q][DHP] (the
+// swizzled 16-bit layout the kernels stage Q and dO in) instead of global
+// memory. W comes from global memory (it is tiny and stays in L1).
+template <typename T, int DH, int C, int CP, int RBD>
+__device__ __forceinline__ void project_staged(const FstProblem& p, const unsigned char* xs,
+                                               int rows_per_head, float mul, int64_t row0,
+                                               int nvalid, int nrows, int h0, int NH,
+                                               unsigned char* tile, T* __restrict__ gdst) {
+  using E = Elem<T>;
+  constexpr int RBC = CP * 2;
+  for (int idx = threadIdx.x; idx < nrows * 16 * (CP / 2); idx += blockDim.x) {
+    const int c2 = idx % (CP / 2), h = (idx / (CP / 2)) % 16, q = idx / (16 * (CP / 2));
+    uint32_t packed = 0u;
+    if (q < nvalid && h < NH && 2 * c2 < C) {
+      const unsigned char* xr = xs + h * rows_per_head * RBD;
+      float a0 = 0.f, a1 = 0.f;
+#pragma unroll
+      for (int ch = 0; ch < DH / 8; ++ch) {
+        const uint4 raw = *(const uint4*)(xr + swz<RBD>(q, ch));
+        const uint32_t* w2 = (const uint32_t*)&raw;
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int d = ch * 8 + 2 * e;
+          const float x0 = E::lo(w2[e]) * mul, x1 = E::hi(w2[e]) * mul;
+          const float2 wa = *(const float2*)(p.weight + (int64_t)d * C + 2 * c2);
+          const float2 wb = *(const float2*)(p.weight + (int64_t)(d + 1) * C + 2 * c2);
+          a0 = fmaf(x0, wa.x, a0);
+          a1 = fmaf(x0, wa.y, a1);
+          a0 = fmaf(x1, wb.x, a0);
+          a1 = fmaf(x1, wb.y, a1);
+        }
+      }
+      packed = E::pack(a0, a1);
+      if (gdst) *(uint32_t*)(gdst + vec_off(p, row0 + q, h0 + h, C) + 2 * c2) = packed;
+    }
+    if (tile) *(uint32_t*)(tile + swz<RBC>(q * 16 + h, c2 / 4) + (c2 % 4) * 4) = packed;
+  }
+}
+
+// Multiply a staged [h][q][DHP] 16-bit tile by `mul` in place, rounding once.
+template <typename T, int DH, int RBD>
+__device__ __forceinline__ void scale_staged(unsigned char* xs, int nheads, int rows_per_head,
+                                             float mul) {
+  using E = Elem<T>;
+  constexpr int CH = DH / 8;
+  for (int idx = threadIdx.x; idx < nheads * rows_per_head * CH; idx += blockDim.x) {
+    const int c = idx % CH, q = (idx / CH) % rows_per_head, h = idx / (CH * rows_per_head);
+    uint4* ptr = (uint4*)(xs + h * rows_per_head * RBD + swz<RBD>(q, c));
+    uint4 v = *ptr;
+    uint32_t* w = (uint32_t*)&v;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) w[k] = E::pack(E::lo(w[k]) * mul, E::hi(w[k]) * mul);
+    *ptr = v;
+  }
+}
+
+// Copy [rows, H, C] rows given by the caller into the same swizzled tile
+// layout project_rows produces.
+template <typename T, int C, int CP>
+__device__ __forceinline__ void stage_rows(const FstProblem& p, const T* __restrict__ src,
+                                           int64_t row0, int nvalid, int nrows, int h0, int NH,
+                                           unsigned char* tile) {
+  constexpr int RBC = CP * 2, UCH = CP / 8;
+  for (int idx = threadIdx.x; idx < nrows * 16 * UCH; idx += blockDim.x) {
+    const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (q < nvalid && h < NH && c * 8 < C)
+      v = *(const uint4*)(src + vec_off(p, row0 + q, h0 + h, C) + c * 8);
+    *(uint4*)(tile + swz<RBC>(q * 16 + h, c)) = v;
+  }
 }
 
 }  // namespace tc

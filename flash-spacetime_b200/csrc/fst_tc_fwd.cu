@@ -189,24 +189,25 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     constexpr int QCH = DH / 8;  // 16-byte chunks per q row
     for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (q < nvalid_q) {
-        const uint4 raw = *(const uint4*)(gq + vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8);
-        const uint32_t* w = (const uint32_t*)&raw;
-        uint32_t* o = (uint32_t*)&v;
-#pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = E::pack(E::lo(w[i]) * p.scale, E::hi(w[i]) * p.scale);
-      }
+      uint4 v = make_uint4(0, 0, 0, 0);  // raw q; scaled in place below
+      if (q < nvalid_q)
+        v = *(const uint4*)(gq + vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8);
       *(uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c)) = v;
     }
-    constexpr int UCH = S::CP / 8;
-    for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
-      const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (attn && q < nvalid_q && h < NH && c * 8 < C)
-        v = *(const uint4*)(gu + vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8);
-      *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = v;
+    if (attn && gu == nullptr) {
+      // u = (q * scale) W computed here, in fp32, from the staged raw q.
+      __syncthreads();
+      project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev.row0 + q0,
+                                              nvalid_q, S::BM, h0, NH, smem + S::OFF_U, nullptr);
+    } else {
+      constexpr int UCH = S::CP / 8;
+      for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
+        const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (attn && q < nvalid_q && h < NH && c * 8 < C)
+          v = *(const uint4*)(gu + vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8);
+        *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = v;
+      }
     }
     // W^T operand of the epilogue, split into hi + lo halves of the 16-bit type
     // so that (A'/l) W^T keeps W at ~fp32 accuracy.
@@ -228,6 +229,8 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
     }
   }
+  __syncthreads();
+  scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();
 
   const int m4 = lane & 3, r8 = lane >> 2;
@@ -270,11 +273,14 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     const int e = warp - NH;
     const int qe = e * S::QPE;  // first query row owned by this warp
     // This lane evaluates frequencies 8g + 2*m4 + r (g < FG, r < 2).
-    float fr[S::FG][2];
+    float fr[S::FG][2], fv[S::FG][2];  // f and f / (2 pi) of this lane's frequencies
 #pragma unroll
     for (int g = 0; g < S::FG; ++g) {
-      fr[g][0] = p.freqs[8 * g + 2 * m4];
-      fr[g][1] = p.freqs[8 * g + 2 * m4 + 1];
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        fr[g][r] = p.freqs[8 * g + 2 * m4 + r];
+        fv[g][r] = fr[g][r] * 0.15915494309189535f;
+      }
     }
     // Coordinates of the query this lane evaluates x for (lane group m4).
     const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
@@ -286,12 +292,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 
     // Private ring of key coordinates: [2 stages][BN][4] fp32.
     const uint32_t c_ring = sC + e * 2 * S::BN * 16;
+    const float* __restrict__ fbase = p.feats + ev.row0 * p.feat_stride;
     auto load_coords = [&](int n) {
       if (n < nchunks && lane < S::BN) {
         const int j = n * S::BN + lane;
         const uint32_t dst = c_ring + ((n & 1) * S::BN + lane) * 16;
         if (j < ev.len)
-          cp_async16(dst, p.feats + (ev.row0 + j) * p.feat_stride);
+          cp_async16(dst, fbase + j * p.feat_stride);
         else
           asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(dst), "r"(0));
       }
@@ -322,7 +329,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         c4.y = ck.y;
         c4.z = ck.z;
         c4.t = ck.w;
-        xl[nt] = pair_angle(cq, c4);
+        xl[nt] = pair_angle_fast(cq, c4);
       }
       __syncwarp();
       load_coords(n + 2);  // stage s is free again
@@ -339,7 +346,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
 #pragma unroll
-            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], sn[nt][g][r], cs[nt][g][r]);
+            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
         }
         // Channel c < F is sin(x f_c); c >= F is cos(x f_{c-F}). The lane's
         // fragment slots are channels 16 ks + 8 hi + 2 m4 + r.
@@ -453,6 +460,11 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     const int hl = warp;  // local head
     const int h = h0 + hl;
     // Private ring of this head's K and V chunks: [2 stages][BN][DHP].
+    // K / V of this head: event base pointer and row stride (no 64-bit math
+    // per copy).
+    const T* __restrict__ kbase = gk + vec_off(p, ev.row0, h, DH);
+    const T* __restrict__ vbase = gv + vec_off(p, ev.row0, h, DH);
+    const int rs = row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
         constexpr int CH = DH / 8;
@@ -463,9 +475,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
           const int c = idx % CH, j = idx / CH;
           const uint32_t off = swz<S::RBD>(j, c);
           if (j0 + j < ev.len) {
-            const int64_t go = vec_off(p, ev.row0 + j0 + j, h, DH) + c * 8;
-            cp_async16(k_st + off, gk + go);
-            cp_async16(v_st + off, gv + go);
+            const int go = (j0 + j) * rs + c * 8;
+            cp_async16(k_st + off, kbase + go);
+            cp_async16(v_st + off, vbase + go);
           } else {
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(k_st + off), "r"(0));
             asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(v_st + off), "r"(0));
@@ -549,45 +561,62 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       }
 
       // Online softmax in the log2 domain (upstream forward.py:170-185).
-      const bool tail = j0 + S::BN > ev.len;
+      // Keys past the event exist only in the last chunk; only that chunk
+      // pays for the mask.
+      if (j0 + S::BN > ev.len) {
+        const int lim = ev.len - j0 - 2 * m4;
+#pragma unroll
+        for (int rg = 0; rg < S::RG; ++rg)
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+            for (int i = 0; i < 4; ++i)
+              if (nt * 8 + (i & 1) >= lim) sc[rg][nt][i] = -INFINITY;
+      }
       uint32_t pa[S::RG][4];
       float alpha[S::RG][2];
+      float mnew[S::RG][2];
+      bool grew = false;
 #pragma unroll
-      for (int rg = 0; rg < S::RG; ++rg) {
-#pragma unroll
-        for (int nt = 0; nt < 2; ++nt)
-#pragma unroll
-          for (int i = 0; i < 4; ++i) {
-            float v = sc[rg][nt][i] * kLog2e;
-            if (tail && j0 + nt * 8 + 2 * m4 + (i & 1) >= ev.len) v = -INFINITY;
-            sc[rg][nt][i] = v;
-          }
+      for (int rg = 0; rg < S::RG; ++rg)
 #pragma unroll
         for (int rh = 0; rh < 2; ++rh) {
           float mx = fmaxf(fmaxf(sc[rg][0][2 * rh], sc[rg][0][2 * rh + 1]),
-                           fmaxf(sc[rg][1][2 * rh], sc[rg][1][2 * rh + 1]));
+                           fmaxf(sc[rg][1][2 * rh], sc[rg][1][2 * rh + 1])) * kLog2e;
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          const float mnew = fmaxf(mrun[rg][rh], mx);
-          const float muse = mnew == -INFINITY ? 0.f : mnew;
-          const float al = ex2(mrun[rg][rh] - muse);
+          mnew[rg][rh] = fmaxf(mrun[rg][rh], mx);
+          grew |= mnew[rg][rh] > mrun[rg][rh];
+        }
+      // The running max only moves now and then after the first chunks; when
+      // it moved for no row of the warp, every rescale factor is exactly 1.
+      const bool rescale = __any_sync(0xffffffffu, grew);
+#pragma unroll
+      for (int rg = 0; rg < S::RG; ++rg) {
+#pragma unroll
+        for (int rh = 0; rh < 2; ++rh) {
+          const float muse = mnew[rg][rh] == -INFINITY ? 0.f : mnew[rg][rh];
           float ps = 0.f;
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
             for (int c = 0; c < 2; ++c) {
-              const float pv = ex2(sc[rg][nt][2 * rh + c] - muse);
+              const float pv = ex2(fmaf(sc[rg][nt][2 * rh + c], kLog2e, -muse));
               sc[rg][nt][2 * rh + c] = pv;
               ps += pv;
             }
-          lrun[rg][rh] = lrun[rg][rh] * al + ps;
-          mrun[rg][rh] = mnew;
-          alpha[rg][rh] = al;
+          float al = 1.f;
+          if (rescale) {
+            al = ex2(mrun[rg][rh] - muse);
 #pragma unroll
-          for (int nd = 0; nd < S::NTD; ++nd) {
-            o[rg][nd][2 * rh] *= al;
-            o[rg][nd][2 * rh + 1] *= al;
+            for (int nd = 0; nd < S::NTD; ++nd) {
+              o[rg][nd][2 * rh] *= al;
+              o[rg][nd][2 * rh + 1] *= al;
+            }
           }
+          lrun[rg][rh] = lrun[rg][rh] * al + ps;
+          mrun[rg][rh] = mnew[rg][rh];
+          alpha[rg][rh] = al;
         }
         pa[rg][0] = E::pack(sc[rg][0][0], sc[rg][0][1]);
         pa[rg][1] = E::pack(sc[rg][0][2], sc[rg][0][3]);
@@ -650,7 +679,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     __syncthreads();
     __syncthreads();  // E warps published R = (A'/l) W^T
 
-    const float* rs = (const float*)(smem + S::OFF_B);
+    const float* rsm = (const float*)(smem + S::OFF_B);
 #pragma unroll
     for (int rg = 0; rg < S::RG; ++rg)
 #pragma unroll
@@ -666,8 +695,8 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
           const int d = nd * 8 + 2 * m4;
           float v0 = o[rg][nd][2 * rh] * il, v1 = o[rg][nd][2 * rh + 1] * il;
           if (act && valid) {
-            v0 += rs[(q * S::HP + hl) * DH + d];
-            v1 += rs[(q * S::HP + hl) * DH + d + 1];
+            v0 += rsm[(q * S::HP + hl) * DH + d];
+            v1 += rsm[(q * S::HP + hl) * DH + d + 1];
             if (p.bias) {
               v0 += p.bias[d];
               v1 += p.bias[d + 1];

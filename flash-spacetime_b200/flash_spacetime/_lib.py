@@ -21,7 +21,7 @@ FST_ERR_CUDA = 3
 FST_ERR_WORKSPACE = 4
 FST_ERR_DEVICE = 5
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 EXPORTED = (
     "fst_abi_version",
@@ -87,6 +87,7 @@ class FstBackwardArgs(ctypes.Structure):
         ("dk", ctypes.c_void_p),
         ("dv", ctypes.c_void_p),
         ("dw_partial", ctypes.c_void_p),
+        ("db_partial", ctypes.c_void_p),
         ("delta", ctypes.c_void_p),
         ("sigma", ctypes.c_void_p),
         ("ds_absmax", ctypes.c_void_p),

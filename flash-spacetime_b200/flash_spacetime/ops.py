@@ -169,7 +169,15 @@ class _Problem:
         self.attn, self.act = bool(use_attn_bias), bool(use_act_bias)
         self.dtype = q.dtype
         self.device = q.device
-        self.feats = feats[..., :4].to(torch.float32).contiguous()
+        # The kernels read x, y, z, t from each feats row at a fixed float
+        # stride; a contiguous fp32 tensor whose row length is a multiple of 4
+        # (16-byte rows) is used in place, anything else is repacked to [.., 4].
+        if feats.dtype == torch.float32 and feats.is_contiguous() and feats.shape[-1] % 4 == 0:
+            self.feats = feats.detach()
+            self.feat_stride = feats.shape[-1]
+        else:
+            self.feats = feats.detach()[..., :4].to(torch.float32).contiguous()
+            self.feat_stride = 4
         self.freqs = _freqs(channels, q.device)
         self.w32 = weight.detach().to(torch.float32).contiguous()
         self.b32 = None if bias is None else bias.detach().to(torch.float32).contiguous()
@@ -183,7 +191,7 @@ class _Problem:
         p.max_len = self.length
         p.head_dim = self.dim
         p.channels = self.channels
-        p.feat_stride = 4
+        p.feat_stride = self.feat_stride
         p.total_rows = self.rows
         p.scale = self.scale
         p.use_attn_bias = int(self.attn)
@@ -200,12 +208,6 @@ class _Problem:
         if self.packed:
             return (self.rows, self.heads)
         return (self.batch, self.heads, self.length)
-
-    def project_queries(self, q: Tensor) -> Optional[Tensor]:
-        """``u = (q * scale) @ W`` in fp32, rounded to q's dtype (forward.py:279-286)."""
-        if not self.attn:
-            return None
-        return ((q.to(torch.float32) * self.scale) @ self.w32).to(q.dtype).contiguous()
 
     def valid_rows(self) -> Optional[Tensor]:
         """``[B, 1, L, 1]`` bool of valid rows (padded layout), else None."""
@@ -224,7 +226,10 @@ def _workspace(nbytes: int, device: torch.device) -> Tuple[Optional[Tensor], int
 def fused_forward(pb: _Problem, q: Tensor, k: Tensor, v: Tensor) -> Tuple[Tensor, Tensor]:
     """One ``fst_forward`` call. Returns ``(out, lse)``."""
     lib = _lib.load()
-    u = pb.project_queries(q)
+    # u = (q * scale) @ W (upstream forward.py:279-286) is formed in fp32 by the
+    # kernels themselves (u = NULL), which saves the host GEMM and its HBM
+    # round trips; the arithmetic is the same fp32 projection rounded once.
+    u = None
     out = torch.empty_like(q)
     lse = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
     a = _lib.FstForwardArgs()
@@ -257,16 +262,15 @@ def fused_backward(
     """
     lib = _lib.load()
     dout = dout.contiguous()
-    u = pb.project_queries(q)
-    wt = None
-    if pb.act:
-        wt = (dout.to(torch.float32) @ pb.w32).to(dout.dtype).contiguous()
+    # u and w~ = dO @ W (upstream backward.py:541-556) are formed in-kernel.
+    u = wt = None
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     a = _lib.FstBackwardArgs()
     a.prob = pb.c_struct()
     nparts = int(lib.fst_dw_partial_count(ctypes.byref(a.prob)))
     dw_part = torch.empty(max(nparts, 1), pb.dim, pb.channels, dtype=torch.float32,
                           device=pb.device)
+    db_part = torch.empty(max(nparts, 1), pb.dim, dtype=torch.float32, device=pb.device)
     delta = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
     sigma = torch.empty_like(delta)
     absmax = torch.empty_like(delta) if want_absmax else None
@@ -274,7 +278,8 @@ def fused_backward(
     a.q, a.k, a.v, a.u, a.out = _ptr(q), _ptr(k), _ptr(v), _ptr(u), _ptr(out)
     a.dout, a.wt, a.lse = _ptr(dout), _ptr(wt), _ptr(lse)
     a.dq, a.dk, a.dv = _ptr(dq), _ptr(dk), _ptr(dv)
-    a.dw_partial, a.delta, a.sigma = _ptr(dw_part), _ptr(delta), _ptr(sigma)
+    a.dw_partial, a.db_partial = _ptr(dw_part), _ptr(db_part)
+    a.delta, a.sigma = _ptr(delta), _ptr(sigma)
     a.ds_absmax = _ptr(absmax)
     a.workspace, a.workspace_bytes = _ptr(ws), nws
     rc = _timed_call("fst_backward", lib.fst_backward, (ctypes.byref(a), _stream(pb.device)),
@@ -286,12 +291,9 @@ def fused_backward(
         dw = dw_part[:nparts].sum(0)
     if pb.b32 is not None:
         if pb.act:
-            rows = dout.to(torch.float32)
-            valid = pb.valid_rows()
-            if valid is not None:
-                rows = torch.where(valid, rows, torch.zeros((), device=pb.device))
-            db = rows.reshape(-1, pb.dim).sum(0)
+            db = db_part[:nparts].sum(0)  # sum of dO over valid rows (backward.py:615-618)
         else:
+            # The logit path's db vanishes analytically (backward.py:619-622).
             db = torch.zeros(pb.dim, dtype=torch.float32, device=pb.device)
     return {"dq": dq, "dk": dk, "dv": dv, "dW": dw, "db": db,
             "delta": delta, "sigma": sigma, "ds_absmax": absmax}

@@ -46,7 +46,7 @@
 extern "C" {
 #endif
 
-#define FST_ABI_VERSION 1
+#define FST_ABI_VERSION 2
 
 /* Storage dtype of q, k, v, u, wt, out, dout, dq, dk, dv. */
 enum FstDtype { FST_F32 = 0, FST_BF16 = 1, FST_F16 = 2 };
@@ -94,7 +94,8 @@ typedef struct FstForwardArgs {
   const void* q;         /* unscaled queries                                 */
   const void* k;
   const void* v;
-  const void* u;         /* (q*scale) @ W rounded to dtype; NULL if !attn    */
+  const void* u;         /* (q*scale) @ W rounded to dtype, or NULL: then the */
+                         /* kernels form it in fp32 themselves               */
   void* out;             /* output, same layout/dtype as q                   */
   float* lse;            /* log-sum-exp of the logits WITHOUT the qt.b term  */
   void* workspace;       /* device scratch, >= fst_forward_workspace_size()  */
@@ -106,17 +107,19 @@ typedef struct FstBackwardArgs {
   const void* q;
   const void* k;
   const void* v;
-  const void* u;         /* as in the forward; NULL if !attn                 */
+  const void* u;         /* as in the forward (NULL: formed in-kernel)       */
   const void* out;       /* forward output; gives the row offset dO.(out-b)  */
                          /* subtracted from dP before summing. May be NULL. */
   const void* dout;      /* upstream gradient, padding rows ignored          */
-  const void* wt;        /* dout @ W rounded to dtype; NULL if !act          */
+  const void* wt;        /* dout @ W rounded to dtype (NULL: formed in-kernel) */
   const float* lse;      /* from fst_forward                                 */
   void* dq;              /* outputs, layout/dtype of q                       */
   void* dk;
   void* dv;
   float* dw_partial;     /* [fst_dw_partial_count(), Dh, C] fp32; the caller */
                          /* sums axis 0 (fixed order) to obtain dW           */
+  float* db_partial;     /* [fst_dw_partial_count(), Dh] fp32: partial sums  */
+                         /* of dout over valid rows (db when act and bias)   */
   float* delta;          /* [rows, H] fp32: D_i = sum P dP / sum P, dP taken */
                          /* without its dO.b row constant (it cancels)       */
   float* sigma;          /* [rows, H] fp32: rowsum(dS), zero by construction */

@@ -68,6 +68,16 @@ int cuda_status(const char* where) {
 
 }  // namespace
 
+namespace fst {
+int api_fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+}  // namespace fst
+
 extern "C" {
 
 int fst_abi_version(void) { return FST_ABI_VERSION; }

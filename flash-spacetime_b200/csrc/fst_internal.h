@@ -8,6 +8,8 @@
 namespace fst {
 // Counts kernel launches made by this library (see fst_kernel_launches).
 void count_launch(int n = 1);
+// Records a formatted error message for fst_last_error and returns `code`.
+int api_fail(int code, const char* fmt, ...);
 namespace simt {
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st);

@@ -30,6 +30,7 @@ EXPORTED = (
     "fst_dw_partial_count",
     "fst_forward",
     "fst_backward",
+    "fst_forward_noalloc",
     "fst_kernel_launches",
     "fst_last_error",
 )
@@ -125,6 +126,8 @@ def load() -> ctypes.CDLL:
         lib.fst_forward.argtypes = [ctypes.POINTER(FstForwardArgs), ctypes.c_void_p]
         lib.fst_backward.restype = ctypes.c_int
         lib.fst_backward.argtypes = [ctypes.POINTER(FstBackwardArgs), ctypes.c_void_p]
+        lib.fst_forward_noalloc.restype = ctypes.c_int
+        lib.fst_forward_noalloc.argtypes = [ctypes.POINTER(FstForwardArgs), ctypes.c_void_p]
         lib.fst_kernel_launches.restype = ctypes.c_int64
         lib.fst_last_error.restype = ctypes.c_int
         lib.fst_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]

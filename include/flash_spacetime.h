@@ -144,6 +144,18 @@ int fst_forward(const FstForwardArgs* args, void* stream);
 /* Fused backward (upstream backward.py:488-630). */
 int fst_backward(const FstBackwardArgs* args, void* stream);
 
+/* fst_forward for callers that cannot allocate device memory (no counterpart
+ * in the upstream package). Inference servers and plugin hosts with a fixed,
+ * pre-reserved memory pool, or real-time loops where a cudaMalloc (which may
+ * synchronise the device) is not allowed, cannot provide fst_forward's
+ * workspace. This variant ignores args->workspace and takes that scratch from
+ * a 256 KiB array built into the library (one per GPU, held until the process
+ * exits); it allocates nothing. Batches of more than 65519 events are
+ * rejected with FST_ERR_INVALID. The first call on a device looks up the
+ * array's address (make it before any stream capture). All calls share the
+ * array: calls that overlap on the GPU race, so order them on one stream. */
+int fst_forward_noalloc(const FstForwardArgs* args, void* stream);
+
 /* Number of CUDA kernels this library has launched in the process so far
  * (benchmark bookkeeping; no counterpart upstream). */
 int64_t fst_kernel_launches(void);

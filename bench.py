@@ -84,9 +84,10 @@ def _workload_lengths(name: str, world: int, rank: int, seed: int):
 
 
 class ClockSampler:
-    """Samples nvidia-smi clocks and throttle reasons during the timed region."""
+    """Samples nvidia-smi clocks and throttle reasons; stop() keeps the samples
+    whose timestamps fall inside the timed region."""
 
-    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
@@ -97,12 +98,12 @@ class ClockSampler:
             ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                 "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except Exception:
             self.proc = None
 
-    def stop(self):
+    def stop(self, t0: float, t1: float):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
@@ -111,23 +112,27 @@ class ClockSampler:
         except Exception:
             self.proc.kill()
             out = ""
-        sm, smax, reasons = [], [], set()
+        import datetime
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        samples = []
         for line in out.strip().splitlines():
             parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
+            if len(parts) < 9:
                 continue
             try:
-                sm.append(float(parts[0]))
-                smax.append(float(parts[1]))
+                ts = datetime.datetime.strptime(parts[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+                samples.append((ts, float(parts[1]), float(parts[2]), parts[5:9]))
             except ValueError:
                 continue
-            for nm, flag in zip(names, parts[4:8]):
-                if flag.lower() == "active":
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(smax) if smax else None,
-                "samples": len(sm), "reasons": sorted(reasons)}
+        inside = [x for x in samples if t0 - 0.06 <= x[0] <= t1 + 0.06]
+        window = "timed region"
+        if not inside:
+            inside, window = samples[-3:], "last samples before stop (timed region shorter than the sampling period)"
+        reasons = sorted({nm for x in inside for nm, flag in zip(names, x[3])
+                          if flag.lower() == "active"})
+        return {"sm_mhz": statistics.median([x[1] for x in inside]) if inside else None,
+                "sm_max_mhz": max([x[2] for x in inside]) if inside else None,
+                "samples": len(inside), "window": window, "reasons": reasons}
 
 
 def cpu_eager_sample(lengths, budget_s: float, seed: int):
@@ -285,6 +290,7 @@ def run_ours(args):
     index = data["seqlens"] if padlen is not None else data["cu_seqlens"]
     timers = []
     ops.set_kernel_timer(timers)
+    clocks = ClockSampler(local)  # started early so it is sampling by the timed region
     for _ in range(args.warmup):
         step(leaves, feats, grad, index)
     torch.cuda.synchronize()
@@ -294,10 +300,10 @@ def run_ours(args):
     base_mem = torch.cuda.memory_allocated(device)
     lib = _lib.load()
     launches0 = lib.fst_kernel_launches()
-    clocks = ClockSampler(local)
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    wall0 = time.time()
     ev0 = torch.cuda.Event(enable_timing=True)
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record()
@@ -307,7 +313,8 @@ def run_ours(args):
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
-    clk = clocks.stop()
+    wall1 = time.time()
+    clk = clocks.stop(wall0, wall1)
     launches = lib.fst_kernel_launches() - launches0
     ms_local = ev0.elapsed_time(ev1) / args.steps
     ms = max_over_ranks(ms_local, device)
@@ -376,7 +383,7 @@ def run_ours(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--workload", default="config1", choices=("config1", "config3", "config4"))

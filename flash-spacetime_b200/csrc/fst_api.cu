@@ -12,6 +12,8 @@
 #include <string.h>
 
 #include <atomic>
+#include <cstdint>
+#include <initializer_list>
 
 #include "fst_internal.h"
 
@@ -57,6 +59,24 @@ int check_problem(const FstProblem* p) {
     return fail(FST_ERR_INVALID, "feats and freqs are required");
   if ((p->use_attn_bias || p->use_act_bias) && p->total_rows > 0 && !p->weight)
     return fail(FST_ERR_INVALID, "weight is required when a bias term is on");
+  return FST_OK;
+}
+
+// The tensor-core kernels move rows with 16-byte vector loads and cp.async,
+// so every row-major tensor they touch must start on a 16-byte boundary and
+// the feature rows must be a whole number of float4s apart.
+bool aligned16(const void* ptr) { return ((uintptr_t)ptr & 15) == 0; }
+
+int check_tc_alignment(const FstProblem& p, std::initializer_list<const void*> ptrs,
+                       const char* what) {
+  if (p.feat_stride % 4)
+    return fail(FST_ERR_INVALID, "%s: feat_stride (=%d) must be a multiple of 4 for 16-bit inputs",
+                what, p.feat_stride);
+  if (!aligned16(p.feats))
+    return fail(FST_ERR_INVALID, "%s: feats must be 16-byte aligned", what);
+  for (const void* ptr : ptrs)
+    if (!aligned16(ptr))
+      return fail(FST_ERR_INVALID, "%s: tensor pointers must be 16-byte aligned", what);
   return FST_OK;
 }
 
@@ -112,6 +132,10 @@ int fst_forward(const FstForwardArgs* a, void* stream) {
   if (need > 0 && (!a->workspace || a->workspace_bytes < need))
     return fail(FST_ERR_WORKSPACE, "forward: workspace %zu bytes < required %zu",
                 a->workspace_bytes, need);
+  if (fst::tc::fwd_supported(p) && p.total_rows > 0) {
+    rc = check_tc_alignment(p, {a->q, a->k, a->v, a->u, a->out, a->workspace}, "forward");
+    if (rc) return rc;
+  }
   cudaGetLastError();  // clear a stale error so the check below is ours
   if (fst::tc::fwd_supported(p)) {
     cudaMemsetAsync(a->workspace, 0, 4, (cudaStream_t)stream);  // device status word
@@ -139,6 +163,11 @@ int fst_backward(const FstBackwardArgs* a, void* stream) {
   if (need > 0 && (!a->workspace || a->workspace_bytes < need))
     return fail(FST_ERR_WORKSPACE, "backward: workspace %zu bytes < required %zu",
                 a->workspace_bytes, need);
+  if (fst::tc::bwd_supported(p) && p.total_rows > 0) {
+    rc = check_tc_alignment(p, {a->q, a->k, a->v, a->u, a->out, a->dout, a->wt, a->dq, a->dk,
+                                a->dv, a->workspace}, "backward");
+    if (rc) return rc;
+  }
   cudaGetLastError();
   if (fst::tc::bwd_supported(p))
     rc = fst::tc::launch_bwd(*a, (cudaStream_t)stream);

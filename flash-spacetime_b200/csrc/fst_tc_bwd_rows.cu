@@ -81,6 +81,7 @@ struct RowShape {
   static constexpr int SMEM = OFF_ST + 3 * BM * HP * 4;
   static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
   static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
+  static_assert(2 * BM * HP * DH * 2 <= 4 * SZ_KV, "staged q, dO fit the K/V ring");
   static constexpr bool kFits = SMEM <= 227 * 1024;
 };
 
@@ -274,13 +275,10 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   __syncthreads();
 
   if (idle) {
-    __syncthreads();
-    __syncthreads();
-    __syncthreads();
-    return;
-  }
-
-  if (warp >= NH) {
+    // Surplus warps of a short head group: no role in the key loop, but they
+    // keep the CTA-wide barrier count and help with the cooperative epilogue.
+    __syncthreads();  // (A)
+  } else if (warp >= NH) {
     // =============================== E warps ==============================
     const int e = warp - NH;
     const int qe = e * S::QPE;
@@ -703,31 +701,48 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       }
     }
   }
-  if (warp >= NH) __syncthreads();  // (B) from the E-warp side
-  __syncthreads();                  // (C) H, G complete for the dW partial
-  // dW partial of this CTA: sum over its valid rows and heads, fixed order.
+  if (warp >= NH) __syncthreads();  // (B) from the E-warp and idle-warp side
+  __syncthreads();  // (C) head warps are done with R; the K/V ring is free
+  // Stage this CTA's raw q and dO rows ([q][head][DH], 16-bit) into the K/V
+  // ring for the dW / db partials below.
+  T* sq = (T*)(smem + S::OFF_K);
+  T* sdo = sq + S::BM * S::HP * DH;
+  {
+    constexpr int CH = DH / 8;
+    for (int idx = threadIdx.x; idx < nvalid_q * NH * CH; idx += nthreads) {
+      const int c = idx % CH, hl = (idx / CH) % NH, q = idx / (CH * NH);
+      const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + hl, DH) + c * 8;
+      const int so = (q * S::HP + hl) * DH + c * 8;
+      *(uint4*)(sq + so) = *(const uint4*)(gq + go);
+      *(uint4*)(sdo + so) = *(const uint4*)(gdo + go);
+    }
+  }
+  __syncthreads();  // (D)
+  // dW partial of this CTA (backward.py:607-614): sum over its valid rows and
+  // heads in a fixed order, qt = q * scale applied once to the q term.
   {
     const float* fH = (const float*)(smem + S::OFF_H);
     const float* fG = (const float*)(smem + S::OFF_G);
     for (int o = threadIdx.x; o < DH * C; o += nthreads) {
       const int d = o / C, c = o - d * C;
-      float acc = 0.f;
+      float aq = 0.f, ad = 0.f;
       for (int q = 0; q < nvalid_q; ++q) {
-        const int64_t row = ev.row0 + q0 + q;
+        const T* xq = sq + q * S::HP * DH + d;
+        const T* xd = sdo + q * S::HP * DH + d;
+        const float* hq = fH + q * S::HP * C + c;
+        const float* gqv = fG + q * S::HP * C + c;
         for (int hl = 0; hl < NH; ++hl) {
-          const int64_t go = vec_off(p, row, h0 + hl, DH) + d;
-          if (attn) acc = fmaf(to_f<T>(gq[go]) * p.scale, fH[(q * S::HP + hl) * C + c], acc);
-          if (act) acc = fmaf(to_f<T>(gdo[go]), fG[(q * S::HP + hl) * C + c], acc);
+          if (attn) aq = fmaf(to_f<T>(xq[hl * DH]), hq[hl * C], aq);
+          if (act) ad = fmaf(to_f<T>(xd[hl * DH]), gqv[hl * C], ad);
         }
       }
-      dwp[o] = acc;
+      dwp[o] = aq * p.scale + ad;
     }
     // db partial: sum of dO over the valid rows and heads (backward.py:615-622).
     for (int d = threadIdx.x; d < DH; d += nthreads) {
       float acc = 0.f;
       for (int q = 0; q < nvalid_q; ++q)
-        for (int hl = 0; hl < NH; ++hl)
-          acc += to_f<T>(gdo[vec_off(p, ev.row0 + q0 + q, h0 + hl, DH) + d]);
+        for (int hl = 0; hl < NH; ++hl) acc += to_f<T>(sdo[(q * S::HP + hl) * DH + d]);
       dbp[d] = acc;
     }
   }

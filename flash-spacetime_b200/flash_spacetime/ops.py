@@ -80,6 +80,13 @@ def _ptr(t: Optional[Tensor]) -> Optional[int]:
     return None if t is None else t.data_ptr()
 
 
+def _dense(t: Tensor) -> Tensor:
+    """``t`` contiguous and starting on a 16-byte boundary (the kernels move
+    rows with 16-byte vector loads); a misaligned view is copied."""
+    t = t.contiguous()
+    return t if t.data_ptr() % 16 == 0 else t.clone()
+
+
 def _stream(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -172,7 +179,8 @@ class _Problem:
         # The kernels read x, y, z, t from each feats row at a fixed float
         # stride; a contiguous fp32 tensor whose row length is a multiple of 4
         # (16-byte rows) is used in place, anything else is repacked to [.., 4].
-        if feats.dtype == torch.float32 and feats.is_contiguous() and feats.shape[-1] % 4 == 0:
+        if (feats.dtype == torch.float32 and feats.is_contiguous() and feats.shape[-1] % 4 == 0
+                and feats.data_ptr() % 16 == 0):
             self.feats = feats.detach()
             self.feat_stride = feats.shape[-1]
         else:
@@ -261,7 +269,7 @@ def fused_backward(
     delta (D), sigma (rowsum dS) and, on request, rowmax |dS|.
     """
     lib = _lib.load()
-    dout = dout.contiguous()
+    dout, out, lse = _dense(dout), _dense(out), lse.contiguous()
     # u and w~ = dO @ W (upstream backward.py:541-556) are formed in-kernel.
     u = wt = None
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
@@ -325,7 +333,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             raise ValueError("q, k and v must have the same dtype")
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
                       use_attn_bias, use_activation_bias)
-        qc, kc, vc = (t.contiguous() for t in (q, k, v))
+        qc, kc, vc = (_dense(t) for t in (q, k, v))
         out, lse = fused_forward(pb, qc, kc, vc)
         ctx.save_for_backward(qc, kc, vc, out, lse)
         ctx.pb = pb
@@ -429,7 +437,7 @@ def flash_spacetime_forward(
     """Forward only, returning ``(out, lse)`` (upstream forward.py:222-346)."""
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
                   use_attn_bias, use_activation_bias)
-    return fused_forward(pb, q.contiguous(), k.contiguous(), v.contiguous())
+    return fused_forward(pb, _dense(q), _dense(k), _dense(v))
 
 
 def flash_spacetime_backward(
@@ -456,5 +464,5 @@ def flash_spacetime_backward(
     """
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
                   use_attn_bias, use_activation_bias)
-    return fused_backward(pb, q.contiguous(), k.contiguous(), v.contiguous(),
+    return fused_backward(pb, _dense(q), _dense(k), _dense(v),
                           out, lse, grad_out, want_absmax)

@@ -70,3 +70,31 @@ def test_struct_layout_matches_header():
         assert int(got[name]) == ctypes.sizeof(cls), name
         for field, _ in cls._fields_:
             assert int(got[f"{name}.{field}"]) == getattr(cls, field).offset, f"{name}.{field}"
+
+
+@pytest.mark.parametrize("which", ["q", "feats", "stride"])
+def test_misaligned_tensor_core_inputs_are_rejected(which):
+    # The tensor-core path moves rows with 16-byte loads; a misaligned pointer
+    # or feature stride must come back as an error before anything launches.
+    # The pointers are never dereferenced: validation returns first.
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.packed, p.batch, p.heads, p.max_len = 1, 0, 1, 1, 16
+    p.head_dim, p.channels, p.feat_stride, p.total_rows = 32, 16, 4, 16
+    p.scale, p.use_attn_bias, p.use_act_bias = 0.25, 1, 1
+    base = 1 << 20
+    p.seqlens, p.feats, p.freqs, p.weight = base, base, base, base
+    a = _lib.FstForwardArgs()
+    a.prob = p
+    a.q = a.k = a.v = a.out = a.lse = a.workspace = base
+    a.workspace_bytes = 1 << 16
+    if which == "q":
+        a.q = base + 2
+    elif which == "feats":
+        a.prob.feats = base + 4
+    else:
+        a.prob.feat_stride = 5
+    rc = lib.fst_forward(ctypes.byref(a), None)
+    assert rc == _lib.FST_ERR_INVALID
+    msg = _lib.last_error()
+    assert ("16-byte" in msg) or ("multiple of 4" in msg), msg

@@ -235,3 +235,18 @@ def test_grad_none_conventions() -> None:
         assert (kg["bias"] is not None) == used
         if flags == (True, False):
             assert torch.equal(kg["bias"], torch.zeros_like(kg["bias"]))
+
+
+@pytest.mark.parametrize("heads", [13, 25])
+def test_uneven_head_groups(heads):
+    """More heads than one CTA holds, split into groups of unequal size."""
+    case = cs.padded_case(2, 50, heads, 32, 16, True, seed=_seed(13, heads))
+    dtype = torch.bfloat16
+    out, _ = _forward(case, (True, True), dtype)
+    kg = _kernel_grads(case, (True, True), dtype)
+    ref = cs.eager_padded(case, (True, True), torch.float64, grad=True)
+    assert cs.normwise(cs.valid_values(out.cpu(), case), cs.valid_values(ref["out"], case)) <= 2e-2
+    for key, rk in (("q", "dq"), ("k", "dk"), ("v", "dv")):
+        assert cs.normwise(cs.valid_values(kg[key], case), cs.valid_values(ref[rk], case)) <= 2e-2, key
+    for key, rk in (("weight", "dW"), ("bias", "db")):
+        assert cs.normwise(kg[key], ref[rk]) <= 2e-2, key

@@ -174,3 +174,38 @@ def test_single_pulse_events():
     single = torch.tensor([0, 1, 7])  # rows of the length-1 events
     torch.testing.assert_close(out[single], ref["out"][single], atol=1e-6, rtol=1e-6)
     torch.testing.assert_close(out, ref["out"], atol=5e-3, rtol=1e-3)
+
+
+def _misaligned(t):
+    # A view of the same values that starts one element into a larger buffer
+    # (two if one element still lands on a 16-byte boundary), so its data
+    # pointer is not 16-byte aligned.
+    buf = torch.empty(t.numel() + 2, dtype=t.dtype, device=t.device)
+    off = 1 if (buf.data_ptr() + t.element_size()) % 16 else 2
+    view = buf[off:off + t.numel()].view(t.shape)
+    view.copy_(t)
+    return view
+
+
+def test_misaligned_views_match_aligned():
+    # Callers may hand over views that start mid-buffer; the public ops must
+    # give the same results as for freshly allocated tensors.
+    case = cs.packed_case([40, 130, 9], 12, 32, 16, seed=77)
+    dtype = torch.bfloat16
+    go = torch.randn(case["q"].shape, generator=torch.Generator().manual_seed(5)).to("cuda", dtype)
+    results = []
+    for shift in (0, 1):
+        q, k, v = (_to(case[x], dtype) for x in ("q", "k", "v"))
+        feats = case["feats"].cuda()
+        if shift:
+            q, k, v = (_misaligned(t) for t in (q, k, v))
+            feats = _misaligned(feats)
+            assert q.data_ptr() % 16 and feats.data_ptr() % 16
+        q.requires_grad_(True)
+        w = _to(case["weight"], torch.float32).requires_grad_(True)
+        out = flash_spacetime_attention_varlen(q, k, v, feats, w, _to(case["bias"], torch.float32),
+                                               case["cu"].cuda())
+        out.backward(_misaligned(go) if shift else go)
+        results.append((out.detach().clone(), q.grad.clone(), w.grad.clone()))
+    for a, b in zip(results[0], results[1]):
+        assert torch.equal(a, b)

@@ -89,6 +89,18 @@ int cuda_status(const char* where) {
 }  // namespace
 
 namespace fst {
+int allow_dynamic_smem(const void* fn, int bytes, std::atomic<uint64_t>& done) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  const uint64_t bit = dev < 64 ? (uint64_t{1} << dev) : 0;
+  if (bit && (done.load(std::memory_order_acquire) & bit)) return 0;
+  e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return (int)e;
+  done.fetch_or(bit, std::memory_order_release);
+  return 0;
+}
+
 int api_fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);

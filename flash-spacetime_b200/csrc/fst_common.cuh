@@ -38,9 +38,15 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) {
 
 // Where one event lives. `row0` is the flat row of the event's first token in
 // the [rows] index space (padded: b*L, packed: cu[b]); `len` its valid length.
+// `base1`, `hs1` and `rs1` address its rows without any division: element
+// (i, h, 0) of a per-row-per-head tensor with `dim` elements per (row, head)
+// sits at (base1 + h*hs1 + i*rs1) * dim (ev_off).
 struct EventSpan {
   int64_t row0;
   int len;
+  int64_t base1;  // (event, head 0, row 0) in units of dim
+  int64_t hs1;    // head stride in units of dim: packed 1, padded L
+  int rs1;        // row stride in units of dim: packed H, padded 1
 };
 
 __device__ __forceinline__ EventSpan event_span(const FstProblem& p, int b) {
@@ -49,11 +55,23 @@ __device__ __forceinline__ EventSpan event_span(const FstProblem& p, int b) {
     int s0 = p.cu_seqlens[b];
     e.row0 = s0;
     e.len = p.cu_seqlens[b + 1] - s0;
+    e.base1 = (int64_t)s0 * p.heads;
+    e.hs1 = 1;
+    e.rs1 = p.heads;
   } else {
     e.row0 = (int64_t)b * p.max_len;
     e.len = p.seqlens[b];
+    e.base1 = (int64_t)b * p.heads * p.max_len;
+    e.hs1 = p.max_len;
+    e.rs1 = 1;
   }
   return e;
+}
+
+// Element offset of (row i of the event, head h, 0) in a [*, H, dim] (packed)
+// or [B, H, L, dim] (padded) tensor.
+__device__ __forceinline__ int64_t ev_off(const EventSpan& e, int i, int h, int dim) {
+  return (e.base1 + h * e.hs1 + (int64_t)i * e.rs1) * dim;
 }
 
 // Event that owns packed row t: the largest b with cu[b] <= t (binary search).

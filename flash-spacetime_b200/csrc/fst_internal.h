@@ -3,6 +3,9 @@
 
 #include <cuda_runtime.h>
 
+#include <atomic>
+#include <cstdint>
+
 #include "../../include/flash_spacetime.h"
 
 namespace fst {
@@ -10,6 +13,9 @@ namespace fst {
 void count_launch(int n = 1);
 // Records a formatted error message for fst_last_error and returns `code`.
 int api_fail(int code, const char* fmt, ...);
+// Raises `fn`'s dynamic shared memory limit to `bytes` on the current device,
+// once per device (bit d of `done`); returns 0 or a cudaError_t.
+int allow_dynamic_smem(const void* fn, int bytes, std::atomic<uint64_t>& done);
 namespace simt {
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st);

@@ -126,7 +126,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       for (int idx = threadIdx.x; idx < NH * S::BK; idx += nthreads) {
         const int h = h0 + idx / S::BK, j = k0 + idx % S::BK;
         if (j >= p.max_len) continue;
-        const int64_t off = vec_off(p, ev.row0 + j, h, DH);
+        const int64_t off = ev_off(ev, j, h, DH);
         for (int d = 0; d < DH; ++d) gdk[off + d] = gdv[off + d] = from_f<T>(0.f);
       }
     }
@@ -145,7 +145,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       const int c = idx % CH, j = (idx / CH) % S::BK, h = idx / (CH * S::BK);
       uint4 vk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
       if (j < nvalid_k) {
-        const int64_t go = vec_off(p, ev.row0 + k0 + j, h0 + h, DH) + c * 8;
+        const int64_t go = ev_off(ev, k0 + j, h0 + h, DH) + c * 8;
         vk = *(const uint4*)(gk + go);
         vv = *(const uint4*)(gv + go);
       }
@@ -201,7 +201,6 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       ck[nt].t = fKC[j * 4 + 3];
     }
     const uint32_t ring = sm + S::OFF_ER + e * 2 * S::SZ_ER;
-    const int rsc = row_stride(p, C);
     const float* __restrict__ fbase = p.feats + ev.row0 * p.feat_stride;
     auto load_ring = [&](int n) {
       if (n < nchunks) {
@@ -212,7 +211,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
           const int i = n * S::BQ + e * S::QPE + t;
           const uint32_t off = swz<S::RBC>(t * S::HP + h, c);
           if (i < ev.len) {
-            const int64_t go = vec_off(p, ev.row0, h0 + h, C) + (int64_t)i * rsc + c * 8;
+            const int64_t go = ev_off(ev, i, h0 + h, C) + c * 8;
             if (attn) cp_async16(st + off, gu + go);
             if (act) cp_async16(st + S::UW + off, gwt + go);
           } else {
@@ -324,9 +323,11 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   const int hl = warp;
   const int h = h0 + hl;
   const uint32_t ring = sm + S::OFF_HR + hl * 2 * S::SZ_HR;
-  const T* __restrict__ qbase = gq + vec_off(p, ev.row0, h, DH);
-  const T* __restrict__ dobase = gdo + vec_off(p, ev.row0, h, DH);
+  const T* __restrict__ qbase = gq + ev_off(ev, 0, h, DH);
+  const T* __restrict__ dobase = gdo + ev_off(ev, 0, h, DH);
   const int rs = row_stride(p, DH);
+  const float* __restrict__ lse_h = a.lse + ev_off(ev, 0, h, 1);  // row qi at qi * ev.rs1
+  const float* __restrict__ delta_h = a.delta + ev_off(ev, 0, h, 1);
   auto load_ring = [&](int n) {
     if (n < nchunks) {
       const uint32_t st = ring + (n & 1) * S::SZ_HR;
@@ -349,9 +350,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
         const int qi = n * S::BQ + lane;
         float l2 = 0.f, dl = 0.f;
         if (qi < ev.len) {
-          const int64_t so = stat_off(p, ev.row0 + qi, h);
-          l2 = a.lse[so] * kLog2e;
-          dl = a.delta[so];
+          l2 = lse_h[qi * ev.rs1] * kLog2e;
+          dl = delta_h[qi * ev.rs1];
         }
         float* f = (float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
         f[lane] = l2;
@@ -487,7 +487,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
           v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));
           const int qi = i0 + nt * 8 + 2 * m4 + c;
           if (r8 == 0 && qi < ev.len)
-            atomicMax((int*)&a.ds_absmax[stat_off(p, ev.row0 + qi, h)], __float_as_int(v));
+            atomicMax((int*)&a.ds_absmax[ev_off(ev, qi, h, 1)], __float_as_int(v));
         }
     }
     // dV += P^T dO, dK += dS^T qt (B fragments: k = query, n = head dim).
@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     const int j = r8 + 8 * rh;
     const bool valid = j < nvalid_k;
     if (!valid && (p.packed || k0 + j >= p.max_len)) continue;
-    const int64_t off = vec_off(p, ev.row0 + k0 + j, h, DH);
+    const int64_t off = ev_off(ev, k0 + j, h, DH);
 #pragma unroll
     for (int nd = 0; nd < S::NTD; ++nd) {
       const int d = nd * 8 + 2 * m4;
@@ -542,14 +542,9 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   if constexpr (!S::kFits) {
     return FST_ERR_UNSUPPORTED;
   } else {
-    static bool configured = false;
-    if (!configured) {
-      if (cudaFuncSetAttribute(bwd_cols_tc_kernel<T, DH, C>,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               S::SMEM) != cudaSuccess)
-        return FST_ERR_CUDA;
-      configured = true;
-    }
+    static std::atomic<uint64_t> configured{0};
+    if (allow_dynamic_smem((const void*)bwd_cols_tc_kernel<T, DH, C>, S::SMEM, configured))
+      return FST_ERR_CUDA;
     const int groups = (p.heads + S::HP - 1) / S::HP;
     const int per_group = (p.heads + groups - 1) / groups;
     const int threads = (per_group + S::NE) * 32;

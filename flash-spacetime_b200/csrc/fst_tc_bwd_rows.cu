@@ -43,6 +43,10 @@ struct RowShape {
   static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1);
   static constexpr int NE = BM / QPE;
   static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;  // heads per CTA
+  // E warps run one chunk ahead (two E fragments live). Their u / w~
+  // A-fragments are then re-read from a resident staged tile each chunk
+  // instead of being held in registers.
+  static constexpr bool AHEAD = C <= 16 && DH <= 32;
   static constexpr int NWARPS = HP + NE;
   static constexpr int KSD = DH / 16, NTD = DH / 8;
   static constexpr int KSC = C / 16, NTC = C / 8;
@@ -67,7 +71,7 @@ struct RowShape {
   static constexpr int SZ_A = 2 * SZ_QS > 2 * SZ_US ? 2 * SZ_QS : 2 * SZ_US;
   static constexpr int SZ_B2 = SZ_LOOP > SZ_HG ? SZ_LOOP : SZ_HG;
   static constexpr int SZ_UNION = SZ_A > SZ_B2 ? SZ_A : SZ_B2;
-  static constexpr int OFF_Q = 0, OFF_DO = SZ_QS, OFF_U = 0, OFF_WT = SZ_US;
+  static constexpr int OFF_Q = 0, OFF_DO = SZ_QS;
   static constexpr int OFF_B = 0, OFF_P = 2 * SZ_B;
   static constexpr int OFF_H = 0, OFF_G = BM * HP * C * 4;
   static constexpr int OFF_W = SZ_UNION;
@@ -78,7 +82,10 @@ struct RowShape {
   static constexpr int OFF_C = OFF_V + 2 * SZ_KV;           // [NE][2][BN][4]
   static constexpr int OFF_QC = OFF_C + NE * 2 * BN * 16;   // [BM][4]
   static constexpr int OFF_ST = OFF_QC + BM * 16;           // lse2, coff, D' : [3][BM][HP]
-  static constexpr int SMEM = OFF_ST + 3 * BM * HP * 4;
+  static constexpr int OFF_UWR = OFF_ST + 3 * BM * HP * 4;  // resident u, w~ (AHEAD)
+  static constexpr int OFF_U = AHEAD ? OFF_UWR : 0;
+  static constexpr int OFF_WT = OFF_U + SZ_US;
+  static constexpr int SMEM = OFF_UWR + (AHEAD ? 2 * SZ_US : 0);
   static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
   static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
   static_assert(2 * BM * HP * DH * 2 <= 4 * SZ_KV, "staged q, dO fit the K/V ring");
@@ -148,10 +155,9 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
         const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
         if (q >= p.max_len) continue;
-        const int64_t row = ev.row0 + q;
-        T* o = gdq + vec_off(p, row, h, DH);
+        T* o = gdq + ev_off(ev, q, h, DH);
         for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
-        const int64_t so = stat_off(p, row, h);
+        const int64_t so = ev_off(ev, q, h, 1);
         a.delta[so] = 0.f;
         a.sigma[so] = 0.f;
       }
@@ -174,7 +180,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
       uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
       if (q < nvalid_q) {  // raw q (scaled in place after the projections)
-        const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8;
+        const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
         vq = *(const uint4*)(gq + go);
         vd = *(const uint4*)(gdo + go);
       }
@@ -184,14 +190,46 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     }
   }
   __syncthreads();
+  // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b),
+  // dO from the staged tile and out with 16-byte loads (d in order).
+  for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
+    const int q = idx / NH, h = idx % NH;
+    float l2 = 0.f, c = 0.f;
+    if (q < nvalid_q) {
+      l2 = a.lse[ev_off(ev, q0 + q, h0 + h, 1)] * kLog2e;
+      if (gout) {
+        const T* orow = gout + ev_off(ev, q0 + q, h0 + h, DH);
+        const unsigned char* drow = smem + S::OFF_DO + h * S::BM * S::RBD;
+#pragma unroll
+        for (int ch = 0; ch < DH / 8; ++ch) {
+          const uint4 ov = *(const uint4*)(orow + ch * 8);
+          const uint4 dv = *(const uint4*)(drow + swz<S::RBD>(q, ch));
+          const uint32_t* o2 = (const uint32_t*)&ov;
+          const uint32_t* d2 = (const uint32_t*)&dv;
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            float o0 = E::lo(o2[e]), o1 = E::hi(o2[e]);
+            if (act && p.bias) {
+              o0 -= p.bias[ch * 8 + 2 * e];
+              o1 -= p.bias[ch * 8 + 2 * e + 1];
+            }
+            c = fmaf(E::lo(d2[e]), o0, c);
+            c = fmaf(E::hi(d2[e]), o1, c);
+          }
+        }
+      }
+    }
+    fLse[q * S::HP + h] = l2;
+    fCoff[q * S::HP + h] = c;
+  }
   // u = (q * scale) W and w~ = dO W in fp32 from the staged raw rows, unless
   // the caller passed them; they go to the workspace, where phase 2 below and
   // the column kernel read them.
   if (attn && a.u == nullptr)
-    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev.row0 + q0,
+    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev, q0,
                                             nvalid_q, S::BM, h0, NH, nullptr, u_ws);
   if (act && a.wt == nullptr)
-    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_DO, S::BM, 1.f, ev.row0 + q0,
+    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_DO, S::BM, 1.f, ev, q0,
                                             nvalid_q, S::BM, h0, NH, nullptr, wt_ws);
   __syncthreads();
   scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
@@ -213,11 +251,11 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   __syncthreads();  // phase 2 of the staging reuses the Q / dO bytes
   {
     if (attn)
-      stage_rows<T, C, S::CP>(p, a.u ? (const T*)a.u : u_ws, ev.row0 + q0, nvalid_q, S::BM, h0,
-                              NH, smem + S::OFF_U);
+      stage_rows<T, C, S::CP>(a.u ? (const T*)a.u : u_ws, ev, q0, nvalid_q, S::BM, h0, NH,
+                              smem + S::OFF_U);
     if (act)
-      stage_rows<T, C, S::CP>(p, a.wt ? (const T*)a.wt : wt_ws, ev.row0 + q0, nvalid_q, S::BM,
-                              h0, NH, smem + S::OFF_WT);
+      stage_rows<T, C, S::CP>(a.wt ? (const T*)a.wt : wt_ws, ev, q0, nvalid_q, S::BM, h0, NH,
+                              smem + S::OFF_WT);
     for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
       const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
       float w0 = 0.f, w1 = 0.f;
@@ -235,25 +273,6 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const int q = idx / 4, k = idx % 4;
       fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
     }
-    // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b).
-    for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
-      const int q = idx / NH, h = idx % NH;
-      float l2 = 0.f, c = 0.f;
-      if (q < nvalid_q) {
-        const int64_t row = ev.row0 + q0 + q;
-        l2 = a.lse[stat_off(p, row, h0 + h)] * kLog2e;
-        if (gout) {
-          const int64_t go = vec_off(p, row, h0 + h, DH);
-          for (int d = 0; d < DH; ++d) {
-            float od = to_f<T>(gout[go + d]);
-            if (act && p.bias) od -= p.bias[d];
-            c = fmaf(to_f<T>(gdo[go + d]), od, c);
-          }
-        }
-      }
-      fLse[q * S::HP + h] = l2;
-      fCoff[q * S::HP + h] = c;
-    }
   }
   __syncthreads();
   if (warp >= NH && !idle) {
@@ -265,8 +284,10 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         const int mi = lane >> 3;
         const int h = (mi & 1) * 8 + (lane & 7);
         const uint32_t off = swz<S::RBC>((qe + t) * 16 + h, 2 * ks + (mi >> 1));
-        ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
-        ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+        if (!S::AHEAD) {
+          ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
+          ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+        }
       }
   }
   __syncthreads();
@@ -321,7 +342,12 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) hacc[t][nc][i] = gacc[t][nc][i] = 0.f;
 
-    for (int n = 0; n < nchunks; ++n) {
+    // With S::AHEAD the E warps run one chunk ahead: chunk n+1's embedding
+    // and bias are produced before waiting for the head warps' P of chunk n,
+    // so the head warps' work on chunk n overlaps the embedding of chunk n+1.
+    using EFrag = uint32_t[S::QPE][2][S::KSC][2];  // E B-fragments (k = channel, n = key)
+    // Embedding of chunk n into eb and its (u.E, w~.E) bias into stage n & 1.
+    auto produce = [&](int n, EFrag& eb) {
       const int s = n & 1;
       cp_async_wait<1>();
       __syncwarp();
@@ -340,7 +366,6 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       __syncwarp();
       load_coords(n + 2);
 
-      uint32_t eb[S::QPE][2][S::KSC][2];
       if (n >= 2) named_sync(rb_bias_empty(s), NBAR);
 #pragma unroll
       for (int t = 0; t < S::QPE; ++t) {
@@ -366,6 +391,16 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
                                           is_sin ? sn[nt][g][1] : cs[nt][g][1]);
             }
         const int q = qe + t;
+        if constexpr (S::AHEAD) {
+#pragma unroll
+          for (int ks = 0; ks < S::KSC; ++ks) {
+            const int mi = lane >> 3;
+            const int h = (mi & 1) * 8 + (lane & 7);
+            const uint32_t off = swz<S::RBC>(q * 16 + h, 2 * ks + (mi >> 1));
+            if (attn) ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
+            if (act) ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+          }
+        }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
           float du[4] = {0.f, 0.f, 0.f, 0.f}, dw[4] = {0.f, 0.f, 0.f, 0.f};
@@ -385,7 +420,10 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         }
       }
       named_arrive(rb_bias_full(s), NBAR);
-
+    };
+    // H' += [P dP'] E and G += [P] E for chunk n.
+    auto consume = [&](int n, const EFrag& eb) {
+      const int s = n & 1;
       named_sync(rb_p_full(s), NBAR);
 #pragma unroll
       for (int t = 0; t < S::QPE; ++t) {
@@ -408,6 +446,24 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         }
       }
       if (n + 2 < nchunks) named_arrive(rb_p_empty(s), NBAR);
+    };
+
+    if constexpr (S::AHEAD) {
+      EFrag eb0, eb1;
+      produce(0, eb0);
+      for (int n = 0; n < nchunks; n += 2) {
+        if (n + 1 < nchunks) produce(n + 1, eb1);
+        consume(n, eb0);
+        if (n + 1 >= nchunks) break;
+        if (n + 2 < nchunks) produce(n + 2, eb0);
+        consume(n + 1, eb1);
+      }
+    } else {
+      EFrag eb0;
+      for (int n = 0; n < nchunks; ++n) {
+        produce(n, eb0);
+        consume(n, eb0);
+      }
     }
 
     __syncthreads();  // (A) head warps published D'
@@ -490,8 +546,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     const uint32_t v_ring = sm + S::OFF_V + hl * S::BN * S::RBD;
     // K / V of this head: event base pointer and row stride (no 64-bit math
     // per copy).
-    const T* __restrict__ kbase = gk + vec_off(p, ev.row0, h, DH);
-    const T* __restrict__ vbase = gv + vec_off(p, ev.row0, h, DH);
+    const T* __restrict__ kbase = gk + ev_off(ev, 0, h, DH);
+    const T* __restrict__ vbase = gv + ev_off(ev, 0, h, DH);
     const int rs = row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
@@ -676,8 +732,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const int q = r8 + 8 * rh;
       const bool valid = q < nvalid_q;
       if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
-      const int64_t row = ev.row0 + q0 + q;
-      T* orow = gdq + vec_off(p, row, h, DH);
+      T* orow = gdq + ev_off(ev, q0 + q, h, DH);
 #pragma unroll
       for (int nd = 0; nd < S::NTD; ++nd) {
         const int d = nd * 8 + 2 * m4;
@@ -695,7 +750,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         *(uint32_t*)(orow + d) = E::pack(v0, v1);
       }
       if (m4 == 0) {
-        const int64_t so = stat_off(p, row, h);
+        const int64_t so = ev_off(ev, q0 + q, h, 1);
         a.delta[so] = valid ? fCoff[q * S::HP + hl] + dpr[rh] : 0.f;
         a.sigma[so] = valid ? sig[rh] : 0.f;
       }
@@ -711,7 +766,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     constexpr int CH = DH / 8;
     for (int idx = threadIdx.x; idx < nvalid_q * NH * CH; idx += nthreads) {
       const int c = idx % CH, hl = (idx / CH) % NH, q = idx / (CH * NH);
-      const int64_t go = vec_off(p, ev.row0 + q0 + q, h0 + hl, DH) + c * 8;
+      const int64_t go = ev_off(ev, q0 + q, h0 + hl, DH) + c * 8;
       const int so = (q * S::HP + hl) * DH + c * 8;
       *(uint4*)(sq + so) = *(const uint4*)(gq + go);
       *(uint4*)(sdo + so) = *(const uint4*)(gdo + go);
@@ -758,13 +813,9 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   if constexpr (!S::kFits) {
     return FST_ERR_UNSUPPORTED;
   }
-  static bool configured = false;
-  if (!configured) {
-    if (cudaFuncSetAttribute(bwd_rows_tc_kernel<T, DH, C>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize, S::SMEM) != cudaSuccess)
-      return FST_ERR_CUDA;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};
+  if (allow_dynamic_smem((const void*)bwd_rows_tc_kernel<T, DH, C>, S::SMEM, configured))
+    return FST_ERR_CUDA;
   const int groups = (p.heads + S::HP - 1) / S::HP;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;

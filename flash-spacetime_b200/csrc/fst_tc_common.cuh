@@ -218,48 +218,19 @@ __device__ __forceinline__ float pair_angle_fast(const Coord4& a, const Coord4& 
 }
 
 // Projection of a block of rows through the encoder weight, in fp32:
-//   out[q][h][c] = [ sum_d (x[q, h0+h, d] * mul) W[d][c] ]   (x: [rows, H, DH] in T)
+//   out[q][h][c] = [ sum_d (x[q, h0+h, d] * mul) W[d][c] ]
 // rounded once to T -- the same arithmetic as the host-side
 // ((x.float() * mul) @ W).to(dtype) of upstream forward.py:279-286 and
-// backward.py:546-547, up to the order of the DH-term sum. The result goes
-// to a swizzled shared tile [q][16][CP] (head rows >= NH, channels >= C and
-// rows >= nvalid are written as zeros) and, if gdst is given, to global
-// memory in the [rows, H, C] layout of x.
-template <typename T, int DH, int C, int CP>
-__device__ __forceinline__ void project_rows(const FstProblem& p, const T* __restrict__ x,
-                                             float mul, int64_t row0, int nvalid, int nrows,
-                                             int h0, int NH, unsigned char* tile,
-                                             T* __restrict__ gdst) {
-  using E = Elem<T>;
-  constexpr int RBC = CP * 2;
-  for (int idx = threadIdx.x; idx < nrows * 16 * (CP / 2); idx += blockDim.x) {
-    const int c2 = idx % (CP / 2), h = (idx / (CP / 2)) % 16, q = idx / (16 * (CP / 2));
-    uint32_t packed = 0u;
-    if (q < nvalid && h < NH && 2 * c2 < C) {
-      const int64_t row = row0 + q;
-      const T* xr = x + vec_off(p, row, h0 + h, DH);
-      float a0 = 0.f, a1 = 0.f;
-#pragma unroll 8
-      for (int d = 0; d < DH; ++d) {
-        const float xv = to_f<T>(xr[d]) * mul;
-        const float2 w = *(const float2*)(p.weight + (int64_t)d * C + 2 * c2);
-        a0 = fmaf(xv, w.x, a0);
-        a1 = fmaf(xv, w.y, a1);
-      }
-      packed = E::pack(a0, a1);
-      if (gdst) *(uint32_t*)(gdst + vec_off(p, row, h0 + h, C) + 2 * c2) = packed;
-    }
-    *(uint32_t*)(tile + swz<RBC>(q * 16 + h, c2 / 4) + (c2 % 4) * 4) = packed;
-  }
-}
-
-// As project_rows, reading x from a staged shared tile [h][q][DHP] (the
-// swizzled 16-bit layout the kernels stage Q and dO in) instead of global
-// memory. W comes from global memory (it is tiny and stays in L1).
+// backward.py:546-547, up to the order of the DH-term sum. x is read from a
+// staged shared tile [h][q][DHP] (the swizzled 16-bit layout the kernels
+// stage Q and dO in); W comes from global memory (it is tiny and stays in
+// L1). The result goes to a swizzled shared tile [q][16][CP] (head rows >= NH,
+// channels >= C and rows >= nvalid are written as zeros) and, if gdst is
+// given, to global memory in the [rows, H, C] layout, rows i0 + q of event ev.
 template <typename T, int DH, int C, int CP, int RBD>
 __device__ __forceinline__ void project_staged(const FstProblem& p, const unsigned char* xs,
-                                               int rows_per_head, float mul, int64_t row0,
-                                               int nvalid, int nrows, int h0, int NH,
+                                               int rows_per_head, float mul, const EventSpan& ev,
+                                               int i0, int nvalid, int nrows, int h0, int NH,
                                                unsigned char* tile, T* __restrict__ gdst) {
   using E = Elem<T>;
   constexpr int RBC = CP * 2;
@@ -286,7 +257,7 @@ __device__ __forceinline__ void project_staged(const FstProblem& p, const unsign
         }
       }
       packed = E::pack(a0, a1);
-      if (gdst) *(uint32_t*)(gdst + vec_off(p, row0 + q, h0 + h, C) + 2 * c2) = packed;
+      if (gdst) *(uint32_t*)(gdst + ev_off(ev, i0 + q, h0 + h, C) + 2 * c2) = packed;
     }
     if (tile) *(uint32_t*)(tile + swz<RBC>(q * 16 + h, c2 / 4) + (c2 % 4) * 4) = packed;
   }
@@ -310,17 +281,17 @@ __device__ __forceinline__ void scale_staged(unsigned char* xs, int nheads, int 
 }
 
 // Copy [rows, H, C] rows given by the caller into the same swizzled tile
-// layout project_rows produces.
+// layout project_staged produces.
 template <typename T, int C, int CP>
-__device__ __forceinline__ void stage_rows(const FstProblem& p, const T* __restrict__ src,
-                                           int64_t row0, int nvalid, int nrows, int h0, int NH,
+__device__ __forceinline__ void stage_rows(const T* __restrict__ src, const EventSpan& ev,
+                                           int i0, int nvalid, int nrows, int h0, int NH,
                                            unsigned char* tile) {
   constexpr int RBC = CP * 2, UCH = CP / 8;
   for (int idx = threadIdx.x; idx < nrows * 16 * UCH; idx += blockDim.x) {
     const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
     uint4 v = make_uint4(0, 0, 0, 0);
     if (q < nvalid && h < NH && c * 8 < C)
-      v = *(const uint4*)(src + vec_off(p, row0 + q, h0 + h, C) + c * 8);
+      v = *(const uint4*)(src + ev_off(ev, i0 + q, h0 + h, C) + c * 8);
     *(uint4*)(tile + swz<RBC>(q * 16 + h, c)) = v;
   }
 }

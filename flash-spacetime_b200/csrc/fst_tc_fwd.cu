@@ -53,6 +53,9 @@ struct FwdShape {
   static constexpr int BN = 16;                               // keys per chunk
   static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1); // queries per E warp
   static constexpr int NE = BM / QPE;                         // E warps
+  // E warps run one chunk ahead (two E fragments live) where the registers
+  // allow it without spilling.
+  static constexpr bool AHEAD = C <= 16 && DH <= 32;
   static constexpr int HP = kHeadsPerCta;
   static constexpr int NWARPS = HP + NE;                      // max warps per CTA
   static constexpr int KSD = DH / 16, NTD = DH / 8;
@@ -165,10 +168,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
         const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
         if (q >= p.max_len) continue;
-        const int64_t row = ev.row0 + q;
-        T* o = gout + vec_off(p, row, h, DH);
+        T* o = gout + ev_off(ev, q, h, DH);
         for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
-        a.lse[stat_off(p, row, h)] = 0.f;
+        a.lse[ev_off(ev, q, h, 1)] = 0.f;
       }
     }
     return;
@@ -191,13 +193,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
       uint4 v = make_uint4(0, 0, 0, 0);  // raw q; scaled in place below
       if (q < nvalid_q)
-        v = *(const uint4*)(gq + vec_off(p, ev.row0 + q0 + q, h0 + h, DH) + c * 8);
+        v = *(const uint4*)(gq + ev_off(ev, q0 + q, h0 + h, DH) + c * 8);
       *(uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c)) = v;
     }
     if (attn && gu == nullptr) {
       // u = (q * scale) W computed here, in fp32, from the staged raw q.
       __syncthreads();
-      project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev.row0 + q0,
+      project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev, q0,
                                               nvalid_q, S::BM, h0, NH, smem + S::OFF_U, nullptr);
     } else {
       constexpr int UCH = S::CP / 8;
@@ -205,7 +207,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         const int c = idx % UCH, h = (idx / UCH) % 16, q = idx / (UCH * 16);
         uint4 v = make_uint4(0, 0, 0, 0);
         if (attn && q < nvalid_q && h < NH && c * 8 < C)
-          v = *(const uint4*)(gu + vec_off(p, ev.row0 + q0 + q, h0 + h, C) + c * 8);
+          v = *(const uint4*)(gu + ev_off(ev, q0 + q, h0 + h, C) + c * 8);
         *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = v;
       }
     }
@@ -315,7 +317,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
         for (int i = 0; i < 4; ++i) acc[t][nc][i] = 0.f;
 
-    for (int n = 0; n < nchunks; ++n) {
+    // With S::AHEAD the E warps run one chunk ahead of the P.E products: chunk n+1's
+    // embedding and logit bias are produced before waiting for the head
+    // warps' P of chunk n, so the head warps' softmax of chunk n overlaps the
+    // embedding of chunk n+1 instead of following it.
+    using EFrag = uint32_t[S::QPE][2][S::KSC][2];  // E B-fragments (k = channel, n = key)
+    // Embedding of chunk n into eb and (attn) its logit bias into bias stage n & 1.
+    auto produce = [&](int n, EFrag& eb) {
       const int s = n & 1;
       cp_async_wait<1>();
       __syncwarp();
@@ -333,9 +341,6 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       }
       __syncwarp();
       load_coords(n + 2);  // stage s is free again
-      if (!(attn || act)) continue;
-
-      uint32_t eb[S::QPE][2][S::KSC][2];  // E B-fragments: (k = channel, n = key)
       if (attn && n >= 2) named_sync(bar_bias_empty(s), NBAR);
 #pragma unroll
       for (int t = 0; t < S::QPE; ++t) {
@@ -377,35 +382,57 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         }
       }
       if (attn) named_arrive(bar_bias_full(s), NBAR);
-      if (act) {
-        named_sync(bar_p_full(s), NBAR);
+    };
+    // A'_q += P_q E_q for chunk n, after the online-softmax rescale.
+    auto consume = [&](int n, const EFrag& eb) {
+      const int s = n & 1;
+      named_sync(bar_p_full(s), NBAR);
 #pragma unroll
-        for (int t = 0; t < S::QPE; ++t) {
-          const int q = qe + t;
-          const float* alph = (const float*)(smem + S::OFF_A + (s * S::BM + q) * S::HP * 4);
-          const float a0 = r8 < NH ? alph[r8] : 1.f;
-          const float a1 = r8 + 8 < NH ? alph[r8 + 8] : 1.f;
-          uint32_t pa[4];
-          {
-            const int mi = lane >> 3;
-            const int h = (mi & 1) * 8 + (lane & 7);
-            ldsm_x4(sP + s * S::SZ_P + (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4, pa);
-          }
-#pragma unroll
-          for (int nc = 0; nc < S::NTC; ++nc) {
-            acc[t][nc][0] *= a0;
-            acc[t][nc][1] *= a0;
-            acc[t][nc][2] *= a1;
-            acc[t][nc][3] *= a1;
-            // E^T B-fragment (k = key, n = channel) by transposing the 8x8
-            // blocks of the (k = channel, n = key) fragment in registers.
-            uint32_t bt[2];
-            bt[0] = movm_t(eb[t][0][nc >> 1][nc & 1]);
-            bt[1] = movm_t(eb[t][1][nc >> 1][nc & 1]);
-            mma16816<T>(acc[t][nc], pa, bt);
-          }
+      for (int t = 0; t < S::QPE; ++t) {
+        const int q = qe + t;
+        const float* alph = (const float*)(smem + S::OFF_A + (s * S::BM + q) * S::HP * 4);
+        const float a0 = r8 < NH ? alph[r8] : 1.f;
+        const float a1 = r8 + 8 < NH ? alph[r8 + 8] : 1.f;
+        uint32_t pa[4];
+        {
+          const int mi = lane >> 3;
+          const int h = (mi & 1) * 8 + (lane & 7);
+          ldsm_x4(sP + s * S::SZ_P + (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4, pa);
         }
-        if (n + 2 < nchunks) named_arrive(bar_p_empty(s), NBAR);
+#pragma unroll
+        for (int nc = 0; nc < S::NTC; ++nc) {
+          acc[t][nc][0] *= a0;
+          acc[t][nc][1] *= a0;
+          acc[t][nc][2] *= a1;
+          acc[t][nc][3] *= a1;
+          // E^T B-fragment (k = key, n = channel) by transposing the 8x8
+          // blocks of the (k = channel, n = key) fragment in registers.
+          uint32_t bt[2];
+          bt[0] = movm_t(eb[t][0][nc >> 1][nc & 1]);
+          bt[1] = movm_t(eb[t][1][nc >> 1][nc & 1]);
+          mma16816<T>(acc[t][nc], pa, bt);
+        }
+      }
+      if (n + 2 < nchunks) named_arrive(bar_p_empty(s), NBAR);
+    };
+
+    if (attn || act) {
+      if constexpr (S::AHEAD) {
+        EFrag eb0, eb1;
+        produce(0, eb0);
+        for (int n = 0; n < nchunks; n += 2) {
+          if (n + 1 < nchunks) produce(n + 1, eb1);
+          if (act) consume(n, eb0);
+          if (n + 1 >= nchunks) break;
+          if (n + 2 < nchunks) produce(n + 2, eb0);
+          if (act) consume(n + 1, eb1);
+        }
+      } else {
+        EFrag eb0;
+        for (int n = 0; n < nchunks; ++n) {
+          produce(n, eb0);
+          if (act) consume(n, eb0);
+        }
       }
     }
 
@@ -462,8 +489,8 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     // Private ring of this head's K and V chunks: [2 stages][BN][DHP].
     // K / V of this head: event base pointer and row stride (no 64-bit math
     // per copy).
-    const T* __restrict__ kbase = gk + vec_off(p, ev.row0, h, DH);
-    const T* __restrict__ vbase = gv + vec_off(p, ev.row0, h, DH);
+    const T* __restrict__ kbase = gk + ev_off(ev, 0, h, DH);
+    const T* __restrict__ vbase = gv + ev_off(ev, 0, h, DH);
     const int rs = row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
@@ -687,9 +714,8 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         const int q = rg * 16 + r8 + 8 * rh;
         const bool valid = q < nvalid_q;
         if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
-        const int64_t row = ev.row0 + q0 + q;
         const float il = valid ? 1.f / lrun[rg][rh] : 0.f;
-        T* orow = gout + vec_off(p, row, h, DH);
+        T* orow = gout + ev_off(ev, q0 + q, h, DH);
 #pragma unroll
         for (int nd = 0; nd < S::NTD; ++nd) {
           const int d = nd * 8 + 2 * m4;
@@ -706,7 +732,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
           *(uint32_t*)(orow + d) = E::pack(v0, v1);
         }
         if (m4 == 0)
-          a.lse[stat_off(p, row, h)] =
+          a.lse[ev_off(ev, q0 + q, h, 1)] =
               valid ? (mrun[rg][rh] + __log2f(lrun[rg][rh])) * 0.6931471805599453f : 0.f;
       }
     return;
@@ -763,14 +789,9 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
                             int* status) {
   using S = FwdShape<DH, C>;
   const FstProblem& p = a.prob;
-  static bool configured = false;  // per template instance
-  if (!configured) {
-    if (cudaFuncSetAttribute(fwd_tc_kernel<T, DH, C>,
-                             cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             S::SMEM) != cudaSuccess)
-      return FST_ERR_CUDA;
-    configured = true;
-  }
+  static std::atomic<uint64_t> configured{0};  // per template instance, one bit per device
+  if (allow_dynamic_smem((const void*)fwd_tc_kernel<T, DH, C>, S::SMEM, configured))
+    return FST_ERR_CUDA;
   const int groups = (p.heads + S::HP - 1) / S::HP;
   const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
   const int threads = (per_group + S::NE) * 32;

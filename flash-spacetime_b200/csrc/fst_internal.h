@@ -30,9 +30,9 @@ int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
 // written to tile_start[0..B] (one small kernel; no host synchronisation).
 void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st);
 int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, void* u_ws,
-                    void* wt_ws);
+                    void* wt_ws, void* qt_ws);
 int launch_bwd_cols(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, const void* gu,
-                    const void* gwt);
+                    const void* gwt, const void* gqt);
 int64_t rows_partials(const FstProblem& p);
 bool bwd_supported(const FstProblem& p);
 size_t bwd_workspace(const FstProblem& p);

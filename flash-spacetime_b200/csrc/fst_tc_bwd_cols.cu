@@ -85,7 +85,7 @@ template <typename T, int DH, int C>
 __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     bwd_cols_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
                        int heads_per_group, const T* __restrict__ gu,
-                       const T* __restrict__ gwt) {
+                       const T* __restrict__ gwt, const T* __restrict__ gqt) {
   using S = ColShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -114,7 +114,6 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   const int NE = S::NE;
   const int nthreads = blockDim.x;
   const bool attn = p.use_attn_bias != 0, act = p.use_act_bias != 0;
-  const T* __restrict__ gq = (const T*)a.q;
   const T* __restrict__ gk = (const T*)a.k;
   const T* __restrict__ gv = (const T*)a.v;
   const T* __restrict__ gdo = (const T*)a.dout;
@@ -323,7 +322,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   const int hl = warp;
   const int h = h0 + hl;
   const uint32_t ring = sm + S::OFF_HR + hl * 2 * S::SZ_HR;
-  const T* __restrict__ qbase = gq + ev_off(ev, 0, h, DH);
+  const T* __restrict__ qbase = gqt + ev_off(ev, 0, h, DH);  // qt = [q * scale]
   const T* __restrict__ dobase = gdo + ev_off(ev, 0, h, DH);
   const int rs = row_stride(p, DH);
   const float* __restrict__ lse_h = a.lse + ev_off(ev, 0, h, 1);  // row qi at qi * ev.rs1
@@ -363,6 +362,15 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   load_ring(0);
   load_ring(1);
 
+  // This lane's (u, w) words in its head's bias tile: keys r8 (+8), queries
+  // nt*8 + 2 m4 (+1), 16 bytes per key -- the same every chunk.
+  uint32_t boff[2][2];
+#pragma unroll
+  for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh)
+      boff[nt][rh] = (hl * S::HS + bias_word(r8 + 8 * rh, nt * 8 + 2 * m4, S::JS)) * 4;
+
   float dk[S::NTD][4], dv[S::NTD][4];
 #pragma unroll
   for (int nd = 0; nd < S::NTD; ++nd)
@@ -376,20 +384,6 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     __syncwarp();
     const uint32_t st = ring + s * S::SZ_HR;
     const uint32_t q_st = st, do_st = st + S::BQ * S::RBD;
-    // qt = [q * scale], in place: each lane rescales the chunks it copied.
-    {
-      constexpr int CH = DH / 8;
-      for (int idx = lane; idx < S::BQ * CH; idx += 32) {
-        const int c = idx % CH, i = idx / CH;
-        uint4* ptr = (uint4*)(smem + (q_st - sm) + swz<S::RBD>(i, c));
-        uint4 v = *ptr;
-        uint32_t* w = (uint32_t*)&v;
-#pragma unroll
-        for (int k = 0; k < 4; ++k) w[k] = E::pack(E::lo(w[k]) * p.scale, E::hi(w[k]) * p.scale);
-        *ptr = v;
-      }
-    }
-    __syncwarp();
     const float* stat = (const float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
 
     // S^T = K Q^T, dP^T = V dO^T (B fragments: k = head dim, n = query).
@@ -422,16 +416,14 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     named_sync(cb_bias_full(s), NBAR);
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt) {
-      // keys r8 (+8), queries nt*8 + 2 m4 (+1): (u, w) pairs, 16 bytes per key.
-      const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS + hl * S::HS * 4;
-      const int q = nt * 8 + 2 * m4;
+      const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS;
       float4 b0, b1;
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
                    : "=f"(b0.x), "=f"(b0.y), "=f"(b0.z), "=f"(b0.w)
-                   : "r"(base + bias_word(r8, q, S::JS) * 4));
+                   : "r"(base + boff[nt][0]));
       asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];\n"
                    : "=f"(b1.x), "=f"(b1.y), "=f"(b1.z), "=f"(b1.w)
-                   : "r"(base + bias_word(r8 + 8, q, S::JS) * 4));
+                   : "r"(base + boff[nt][1]));
       sc[nt][0] += b0.x;
       dp[nt][0] += b0.y;
       sc[nt][1] += b0.z;
@@ -536,7 +528,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 
 template <typename T, int DH, int C>
 static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
-                             const void* gu, const void* gwt) {
+                             const void* gu, const void* gwt, const void* gqt) {
   using S = ColShape<DH, C>;
   const FstProblem& p = a.prob;
   if constexpr (!S::kFits) {
@@ -558,7 +550,7 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
     }
     if (grid.x == 0 || grid.y == 0) return FST_OK;
     bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
-                                                                 (const T*)gu, (const T*)gwt);
+                                                                 (const T*)gu, (const T*)gwt, (const T*)gqt);
     count_launch();
     return FST_OK;
   }
@@ -566,10 +558,10 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
 
 template <typename T>
 static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, const void* gu,
-                         const void* gwt) {
+                         const void* gwt, const void* gqt) {
   const int D = a.prob.head_dim, C = a.prob.channels;
 #define FST_COLS_CASE(DD, CC) \
-  if (D == DD && C == CC) return launch_cols_shape<T, DD, CC>(a, st, ts, gu, gwt);
+  if (D == DD && C == CC) return launch_cols_shape<T, DD, CC>(a, st, ts, gu, gwt, gqt);
   FST_COLS_CASE(32, 16)
   FST_COLS_CASE(32, 32)
   FST_COLS_CASE(32, 64)
@@ -582,9 +574,10 @@ static int launch_cols_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, con
 }
 
 int launch_bwd_cols(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, const void* gu,
-                    const void* gwt) {
-  if (a.prob.dtype == FST_BF16) return launch_cols_t<__nv_bfloat16>(a, st, tile_start, gu, gwt);
-  if (a.prob.dtype == FST_F16) return launch_cols_t<__half>(a, st, tile_start, gu, gwt);
+                    const void* gwt, const void* gqt) {
+  if (a.prob.dtype == FST_BF16)
+    return launch_cols_t<__nv_bfloat16>(a, st, tile_start, gu, gwt, gqt);
+  if (a.prob.dtype == FST_F16) return launch_cols_t<__half>(a, st, tile_start, gu, gwt, gqt);
   return FST_ERR_UNSUPPORTED;
 }
 
@@ -593,18 +586,22 @@ bool bwd_supported(const FstProblem& p) {
 }
 
 // Workspace: [status 64 B][tile prefix, B+1 ints][u and w~, rows x H x C each
-// in the 16-bit type, 256-byte aligned] -- the row kernel writes the two
-// projections there when the caller did not pass them, the column kernel
-// reads them back.
+// in the 16-bit type, 256-byte aligned][qt = [q * scale], rows x H x Dh in
+// the 16-bit type] -- the row kernel writes the two projections there (when
+// the caller did not pass them) and the scaled q, the column kernel reads
+// them back.
 static size_t ws_proj_offset(const FstProblem& p) {
   return (64 + (size_t)(p.batch + 1) * sizeof(int) + 255) / 256 * 256;
 }
 static size_t ws_proj_bytes(const FstProblem& p) {
   return ((size_t)p.total_rows * p.heads * p.channels * 2 + 255) / 256 * 256;
 }
+static size_t ws_qt_bytes(const FstProblem& p) {
+  return ((size_t)p.total_rows * p.heads * p.head_dim * 2 + 255) / 256 * 256;
+}
 
 size_t bwd_workspace(const FstProblem& p) {
-  return ws_proj_offset(p) + 2 * ws_proj_bytes(p);
+  return ws_proj_offset(p) + 2 * ws_proj_bytes(p) + ws_qt_bytes(p);
 }
 
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st) {
@@ -613,13 +610,14 @@ int launch_bwd(const FstBackwardArgs& a, cudaStream_t st) {
   unsigned char* proj = (unsigned char*)a.workspace + ws_proj_offset(p);
   void* u_ws = proj;
   void* wt_ws = proj + ws_proj_bytes(p);
+  void* qt_ws = proj + 2 * ws_proj_bytes(p);
   if (a.ds_absmax) {
     const int64_t n = p.total_rows * p.heads;
     if (cudaMemsetAsync(a.ds_absmax, 0, n * sizeof(float), st) != cudaSuccess) return FST_ERR_CUDA;
   }
-  int rc = launch_bwd_rows(a, st, tile_start, u_ws, wt_ws);
+  int rc = launch_bwd_rows(a, st, tile_start, u_ws, wt_ws, qt_ws);
   if (rc) return rc;
-  return launch_bwd_cols(a, st, tile_start, a.u ? a.u : u_ws, a.wt ? a.wt : wt_ws);
+  return launch_bwd_cols(a, st, tile_start, a.u ? a.u : u_ws, a.wt ? a.wt : wt_ws, qt_ws);
 }
 
 }  // namespace tc

@@ -100,7 +100,8 @@ __device__ __forceinline__ int rb_p_empty(int s) { return 7 + s; }
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     bwd_rows_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
-                       int heads_per_group, T* __restrict__ u_ws, T* __restrict__ wt_ws) {
+                       int heads_per_group, T* __restrict__ u_ws, T* __restrict__ wt_ws,
+                       T* __restrict__ qt_ws) {
   using S = RowShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -234,6 +235,15 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   __syncthreads();
   scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();
+  {
+    // qt of the valid rows to the workspace, for the column kernel.
+    constexpr int QCH = DH / 8;
+    for (int idx = threadIdx.x; idx < NH * nvalid_q * QCH; idx += nthreads) {
+      const int c = idx % QCH, q = (idx / QCH) % nvalid_q, h = idx / (QCH * nvalid_q);
+      *(uint4*)(qt_ws + ev_off(ev, q0 + q, h0 + h, DH) + c * 8) =
+          *(const uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c));
+    }
+  }
   const int m4 = lane & 3, r8 = lane >> 2;
   const bool idle = warp >= NH + NE;
   uint32_t qa[S::KSD][4], da[S::KSD][4];  // head warps: Q (scaled) and dO, rows on M
@@ -578,7 +588,12 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     for (int nd = 0; nd < S::NTD; ++nd)
 #pragma unroll
       for (int i = 0; i < 4; ++i) X[nd][i] = Y[nd][i] = 0.f;
-    float asum[2] = {0.f, 0.f}, psum[2] = {0.f, 0.f};
+    // Row sums of [P] and [P dP'] as MMAs against a ones B-fragment: the
+    // tensor core adds exactly the rounded values the X / Y products consume,
+    // and every lane ends with the full sums of rows r8 (slot 0) and r8 + 8
+    // (slot 2).
+    float pacc[4] = {0.f, 0.f, 0.f, 0.f}, aacc[4] = {0.f, 0.f, 0.f, 0.f};
+    const uint32_t ones[2] = {E::kOnes, E::kOnes};
 
     for (int n = 0; n < nchunks; ++n) {
       const int s = n & 1;
@@ -662,11 +677,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       pd[1] = E::pack(dp[0][2], dp[0][3]);
       pd[2] = E::pack(dp[1][0], dp[1][1]);
       pd[3] = E::pack(dp[1][2], dp[1][3]);
-      // Row sums of exactly the rounded values the MMAs consume.
-      psum[0] += (E::lo(pp[0]) + E::hi(pp[0])) + (E::lo(pp[2]) + E::hi(pp[2]));
-      psum[1] += (E::lo(pp[1]) + E::hi(pp[1])) + (E::lo(pp[3]) + E::hi(pp[3]));
-      asum[0] += (E::lo(pd[0]) + E::hi(pd[0])) + (E::lo(pd[2]) + E::hi(pd[2]));
-      asum[1] += (E::lo(pd[1]) + E::hi(pd[1])) + (E::lo(pd[3]) + E::hi(pd[3]));
+      mma16816<T>(pacc, pp, ones);
+      mma16816<T>(aacc, pd, ones);
 
       if (n >= 2) named_sync(rb_p_empty(s), NBAR);
       {
@@ -708,11 +720,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     float dpr[2], sig[2];
 #pragma unroll
     for (int rh = 0; rh < 2; ++rh) {
-      float av = asum[rh], pv = psum[rh];
-      av += __shfl_xor_sync(0xffffffffu, av, 1);
-      av += __shfl_xor_sync(0xffffffffu, av, 2);
-      pv += __shfl_xor_sync(0xffffffffu, pv, 1);
-      pv += __shfl_xor_sync(0xffffffffu, pv, 2);
+      const float av = aacc[2 * rh], pv = pacc[2 * rh];
       dpr[rh] = pv > 0.f ? av / pv : 0.f;
       sig[rh] = av - dpr[rh] * pv;
       if (m4 == 0) fDp[(r8 + 8 * rh) * S::HP + hl] = dpr[rh];
@@ -805,9 +813,23 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
 // ---------------------------------------------------------------------------
 
+// Grid of the row kernel for one (Dh, C) shape: (row tiles, events, head
+// groups). Every CTA writes one dW / db partial, so this also sizes the
+// partial buffers (rows_partials).
+template <int DH, int C>
+static dim3 rows_grid(const FstProblem& p) {
+  using S = RowShape<DH, C>;
+  const int groups = (p.heads + S::HP - 1) / S::HP;
+  if (p.packed) {
+    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
+    return dim3((unsigned)upper, 1, groups);
+  }
+  return dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
+}
+
 template <typename T, int DH, int C>
 static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
-                             void* u_ws, void* wt_ws, int64_t* nparts) {
+                             void* u_ws, void* wt_ws, void* qt_ws) {
   using S = RowShape<DH, C>;
   const FstProblem& p = a.prob;
   if constexpr (!S::kFits) {
@@ -816,39 +838,40 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   static std::atomic<uint64_t> configured{0};
   if (allow_dynamic_smem((const void*)bwd_rows_tc_kernel<T, DH, C>, S::SMEM, configured))
     return FST_ERR_CUDA;
-  const int groups = (p.heads + S::HP - 1) / S::HP;
+  const dim3 grid = rows_grid<DH, C>(p);
+  const int groups = (int)grid.z;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;
-  dim3 grid;
-  if (p.packed) {
-    tile_prefix(p, S::BM, tile_start, st);
-    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
-    grid = dim3((unsigned)upper, 1, groups);
-  } else {
-    grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
-  }
-  *nparts = (int64_t)grid.x * grid.y * grid.z;
+  if (p.packed) tile_prefix(p, S::BM, tile_start, st);
   if (grid.x == 0 || grid.y == 0) return FST_OK;
   bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
-                                                                 (T*)u_ws, (T*)wt_ws);
+                                                                 (T*)u_ws, (T*)wt_ws, (T*)qt_ws);
   count_launch();
   return FST_OK;
 }
 
 int64_t rows_partials(const FstProblem& p) {
-  constexpr int BM = 16;
-  const int groups = (p.heads + 11) / 12;
-  if (p.packed) return ((p.total_rows + BM - 1) / BM + p.batch) * groups;
-  return (int64_t)((p.max_len + BM - 1) / BM) * p.batch * groups;
+  const int D = p.head_dim, C = p.channels;
+  dim3 g(0, 0, 0);
+#define FST_ROWS_CASE(DD, CC) \
+  if (D == DD && C == CC) g = rows_grid<DD, CC>(p);
+  FST_ROWS_CASE(32, 16)
+  FST_ROWS_CASE(32, 32)
+  FST_ROWS_CASE(32, 64)
+  FST_ROWS_CASE(64, 32)
+  FST_ROWS_CASE(64, 64)
+  FST_ROWS_CASE(16, 16)
+  FST_ROWS_CASE(48, 48)
+#undef FST_ROWS_CASE
+  return (int64_t)g.x * g.y * g.z;
 }
 
 template <typename T>
 static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, void* u_ws,
-                         void* wt_ws) {
+                         void* wt_ws, void* qt_ws) {
   const int D = a.prob.head_dim, C = a.prob.channels;
-  int64_t np = 0;
 #define FST_ROWS_CASE(DD, CC) \
-  if (D == DD && C == CC) return launch_rows_shape<T, DD, CC>(a, st, ts, u_ws, wt_ws, &np);
+  if (D == DD && C == CC) return launch_rows_shape<T, DD, CC>(a, st, ts, u_ws, wt_ws, qt_ws);
   FST_ROWS_CASE(32, 16)
   FST_ROWS_CASE(32, 32)
   FST_ROWS_CASE(32, 64)
@@ -861,10 +884,11 @@ static int launch_rows_t(const FstBackwardArgs& a, cudaStream_t st, int* ts, voi
 }
 
 int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, void* u_ws,
-                    void* wt_ws) {
+                    void* wt_ws, void* qt_ws) {
   if (a.prob.dtype == FST_BF16)
-    return launch_rows_t<__nv_bfloat16>(a, st, tile_start, u_ws, wt_ws);
-  if (a.prob.dtype == FST_F16) return launch_rows_t<__half>(a, st, tile_start, u_ws, wt_ws);
+    return launch_rows_t<__nv_bfloat16>(a, st, tile_start, u_ws, wt_ws, qt_ws);
+  if (a.prob.dtype == FST_F16)
+    return launch_rows_t<__half>(a, st, tile_start, u_ws, wt_ws, qt_ws);
   return FST_ERR_UNSUPPORTED;
 }
 

@@ -17,6 +17,7 @@ namespace tc {
 
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {
+  static constexpr uint32_t kOnes = 0x3f803f80u;  // (1.0, 1.0)
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -26,6 +27,7 @@ template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ float hi(uint32_t v) { return __uint_as_float(v & 0xffff0000u); }
 };
 template <> struct Elem<__half> {
+  static constexpr uint32_t kOnes = 0x3c003c00u;  // (1.0, 1.0)
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));

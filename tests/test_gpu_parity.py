@@ -237,10 +237,12 @@ def test_grad_none_conventions() -> None:
             assert torch.equal(kg["bias"], torch.zeros_like(kg["bias"]))
 
 
-@pytest.mark.parametrize("heads", [13, 25])
-def test_uneven_head_groups(heads):
-    """More heads than one CTA holds, split into groups of unequal size."""
-    case = cs.padded_case(2, 50, heads, 32, 16, True, seed=_seed(13, heads))
+@pytest.mark.parametrize("heads,dim,channels", [(13, 32, 16), (25, 32, 16), (12, 48, 48),
+                                                (12, 64, 64), (9, 64, 32)])
+def test_uneven_head_groups(heads, dim, channels):
+    """More heads than one CTA holds, split into groups of unequal size (the
+    wide shapes hold 8 heads per CTA in the backward, 12 in the forward)."""
+    case = cs.padded_case(2, 50, heads, dim, channels, True, seed=_seed(13, heads, dim))
     dtype = torch.bfloat16
     out, _ = _forward(case, (True, True), dtype)
     kg = _kernel_grads(case, (True, True), dtype)

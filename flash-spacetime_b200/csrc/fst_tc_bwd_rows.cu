@@ -88,7 +88,7 @@ struct RowShape {
   static constexpr int SMEM = OFF_UWR + (AHEAD ? 2 * SZ_US : 0);
   static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
   static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
-  static_assert(2 * BM * HP * DH * 2 <= 4 * SZ_KV, "staged q, dO fit the K/V ring");
+  static_assert(2 * HP * BM * RBD <= 4 * SZ_KV, "staged q, dO fit the K/V ring");
   static constexpr bool kFits = SMEM <= 227 * 1024;
 };
 
@@ -189,6 +189,21 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       *(uint4*)(smem + S::OFF_Q + off) = vq;
       *(uint4*)(smem + S::OFF_DO + off) = vd;
     }
+    // W as [d][c], split into hi + lo halves of the 16-bit type: operand of
+    // the projections below and of R = H W^T in the epilogue.
+    for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
+      const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
+      float w0 = 0.f, w1 = 0.f;
+      if ((attn || act) && 2 * c2 < C) {
+        w0 = p.weight[(int64_t)d * C + 2 * c2];
+        w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
+      }
+      const uint32_t hi = E::pack(w0, w1);
+      const uint32_t lo = E::pack(w0 - E::lo(hi), w1 - E::hi(hi));
+      const uint32_t off = swz<S::RBC>(d, c2 / 4) + (c2 % 4) * 4;
+      *(uint32_t*)(smem + S::OFF_W + off) = hi;
+      *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
+    }
   }
   __syncthreads();
   // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b),
@@ -223,15 +238,20 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     fLse[q * S::HP + h] = l2;
     fCoff[q * S::HP + h] = c;
   }
-  // u = (q * scale) W and w~ = dO W in fp32 from the staged raw rows, unless
-  // the caller passed them; they go to the workspace, where phase 2 below and
-  // the column kernel read them.
-  if (attn && a.u == nullptr)
-    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev, q0,
-                                            nvalid_q, S::BM, h0, NH, nullptr, u_ws);
-  if (act && a.wt == nullptr)
-    project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_DO, S::BM, 1.f, ev, q0,
-                                            nvalid_q, S::BM, h0, NH, nullptr, wt_ws);
+  // u = (q * scale) W and w~ = dO W from the staged raw rows (one head per
+  // warp, on the tensor cores), unless the caller passed them; they go to the
+  // workspace, where phase 2 below and the column kernel read them.
+  if (warp < NH) {
+    const uint32_t sW = sm + S::OFF_W, sWlo = sW + DH * S::RBC;
+    if (attn && a.u == nullptr)
+      project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_Q + warp * S::BM * S::RBD, sW,
+                                                  sWlo, p.scale, ev, q0, nvalid_q, h0 + warp,
+                                                  warp, nullptr, u_ws);
+    if (act && a.wt == nullptr)
+      project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_DO + warp * S::BM * S::RBD, sW,
+                                                  sWlo, 1.f, ev, q0, nvalid_q, h0 + warp, warp,
+                                                  nullptr, wt_ws);
+  }
   __syncthreads();
   scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();
@@ -266,19 +286,6 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     if (act)
       stage_rows<T, C, S::CP>(a.wt ? (const T*)a.wt : wt_ws, ev, q0, nvalid_q, S::BM, h0, NH,
                               smem + S::OFF_WT);
-    for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
-      const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
-      float w0 = 0.f, w1 = 0.f;
-      if (attn && 2 * c2 < C) {
-        w0 = p.weight[(int64_t)d * C + 2 * c2];
-        w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
-      }
-      const uint32_t hi = E::pack(w0, w1);
-      const uint32_t lo = E::pack(w0 - E::lo(hi), w1 - E::hi(hi));
-      const uint32_t off = swz<S::RBC>(d, c2 / 4) + (c2 % 4) * 4;
-      *(uint32_t*)(smem + S::OFF_W + off) = hi;
-      *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
-    }
     for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
       const int q = idx / 4, k = idx % 4;
       fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
@@ -766,47 +773,87 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   }
   if (warp >= NH) __syncthreads();  // (B) from the E-warp and idle-warp side
   __syncthreads();  // (C) head warps are done with R; the K/V ring is free
-  // Stage this CTA's raw q and dO rows ([q][head][DH], 16-bit) into the K/V
-  // ring for the dW / db partials below.
-  T* sq = (T*)(smem + S::OFF_K);
-  T* sdo = sq + S::BM * S::HP * DH;
+  // Stage this CTA's raw q and dO as [head][row][DHP] swizzled tiles in the
+  // K/V ring (rows past the event are zero) for the dW / db partials.
+  const uint32_t sq = sm + S::OFF_K, sdo = sq + S::HP * S::BM * S::RBD;
   {
     constexpr int CH = DH / 8;
-    for (int idx = threadIdx.x; idx < nvalid_q * NH * CH; idx += nthreads) {
-      const int c = idx % CH, hl = (idx / CH) % NH, q = idx / (CH * NH);
-      const int64_t go = ev_off(ev, q0 + q, h0 + hl, DH) + c * 8;
-      const int so = (q * S::HP + hl) * DH + c * 8;
-      *(uint4*)(sq + so) = *(const uint4*)(gq + go);
-      *(uint4*)(sdo + so) = *(const uint4*)(gdo + go);
+    for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
+      const int c = idx % CH, q = (idx / CH) % S::BM, hl = idx / (CH * S::BM);
+      uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
+      if (q < nvalid_q) {
+        const int64_t go = ev_off(ev, q0 + q, h0 + hl, DH) + c * 8;
+        vq = *(const uint4*)(gq + go);
+        vd = *(const uint4*)(gdo + go);
+      }
+      const uint32_t so = hl * S::BM * S::RBD + swz<S::RBD>(q, c);
+      *(uint4*)(smem + (sq - sm) + so) = vq;
+      *(uint4*)(smem + (sdo - sm) + so) = vd;
     }
   }
   __syncthreads();  // (D)
-  // dW partial of this CTA (backward.py:607-614): sum over its valid rows and
-  // heads in a fixed order, qt = q * scale applied once to the q term.
+  // dW and db partials of this CTA (backward.py:607-622) on the tensor cores,
+  // one (16 d x 8 c) output tile per warp, K running over (head, row) in a
+  // fixed order:
+  //   dW = scale * sum q^T H + sum dO^T G,   db = sum dO  (= dO^T 1),
+  // with q, dO exact in T and H, G split into hi + lo halves of T.
   {
+    constexpr int MT = DH / 16, NTW = C / 8;
     const float* fH = (const float*)(smem + S::OFF_H);
     const float* fG = (const float*)(smem + S::OFF_G);
-    for (int o = threadIdx.x; o < DH * C; o += nthreads) {
-      const int d = o / C, c = o - d * C;
-      float aq = 0.f, ad = 0.f;
-      for (int q = 0; q < nvalid_q; ++q) {
-        const T* xq = sq + q * S::HP * DH + d;
-        const T* xd = sdo + q * S::HP * DH + d;
-        const float* hq = fH + q * S::HP * C + c;
-        const float* gqv = fG + q * S::HP * C + c;
-        for (int hl = 0; hl < NH; ++hl) {
-          if (attn) aq = fmaf(to_f<T>(xq[hl * DH]), hq[hl * C], aq);
-          if (act) ad = fmaf(to_f<T>(xd[hl * DH]), gqv[hl * C], ad);
+    const int nwarps = nthreads >> 5;
+    const int mi = lane >> 3;
+    const uint32_t ones[2] = {E::kOnes, E::kOnes};
+    for (int tile = warp; tile < MT * NTW; tile += nwarps) {
+      const int mt = tile / NTW, nt = tile % NTW;
+      const int c = nt * 8 + r8;  // this lane's B column
+      // A = x^T (m = d, k = row) from the [row][d] tile by transposed loads.
+      const uint32_t aoff = swz<S::RBD>((mi >> 1) * 8 + (lane & 7), 2 * mt + (mi & 1));
+      float aq[4] = {0.f, 0.f, 0.f, 0.f}, ad[4] = {0.f, 0.f, 0.f, 0.f};
+      float ab[4] = {0.f, 0.f, 0.f, 0.f};
+      for (int hl = 0; hl < NH; ++hl) {
+        uint32_t fq[4], fd[4];
+        ldsm_x4_t(sq + hl * S::BM * S::RBD + aoff, fq);
+        ldsm_x4_t(sdo + hl * S::BM * S::RBD + aoff, fd);
+        // B (k = row, n = channel): rows 2 m4 (+1) and 2 m4 + 8 (+1).
+        float hv[4], gv[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int q = 2 * m4 + (i & 1) + 8 * (i >> 1);
+          const bool ok = q < nvalid_q;
+          hv[i] = ok ? fH[(q * S::HP + hl) * C + c] : 0.f;
+          gv[i] = ok ? fG[(q * S::HP + hl) * C + c] : 0.f;
         }
+        if (attn) {
+          uint32_t bh[2], bl[2];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            bh[r] = E::pack(hv[2 * r], hv[2 * r + 1]);
+            bl[r] = E::pack(hv[2 * r] - E::lo(bh[r]), hv[2 * r + 1] - E::hi(bh[r]));
+          }
+          mma16816<T>(aq, fq, bh);
+          mma16816<T>(aq, fq, bl);
+        }
+        if (act) {
+          uint32_t bh[2], bl[2];
+#pragma unroll
+          for (int r = 0; r < 2; ++r) {
+            bh[r] = E::pack(gv[2 * r], gv[2 * r + 1]);
+            bl[r] = E::pack(gv[2 * r] - E::lo(bh[r]), gv[2 * r + 1] - E::hi(bh[r]));
+          }
+          mma16816<T>(ad, fd, bh);
+          mma16816<T>(ad, fd, bl);
+        }
+        if (nt == 0) mma16816<T>(ab, fd, ones);
       }
-      dwp[o] = aq * p.scale + ad;
-    }
-    // db partial: sum of dO over the valid rows and heads (backward.py:615-622).
-    for (int d = threadIdx.x; d < DH; d += nthreads) {
-      float acc = 0.f;
-      for (int q = 0; q < nvalid_q; ++q)
-        for (int hl = 0; hl < NH; ++hl) acc += to_f<T>(sdo[(q * S::HP + hl) * DH + d]);
-      dbp[d] = acc;
+#pragma unroll
+      for (int rh = 0; rh < 2; ++rh) {
+        const int d = mt * 16 + r8 + 8 * rh;
+        const int c0 = nt * 8 + 2 * m4;
+        dwp[d * C + c0] = aq[2 * rh] * p.scale + ad[2 * rh];
+        dwp[d * C + c0 + 1] = aq[2 * rh + 1] * p.scale + ad[2 * rh + 1];
+        if (nt == 0 && m4 == 0) dbp[d] = ab[2 * rh];
+      }
     }
   }
 }

@@ -219,50 +219,77 @@ __device__ __forceinline__ float pair_angle_fast(const Coord4& a, const Coord4& 
   return copysignf(x, iv);
 }
 
-// Projection of a block of rows through the encoder weight, in fp32:
-//   out[q][h][c] = [ sum_d (x[q, h0+h, d] * mul) W[d][c] ]
-// rounded once to T -- the same arithmetic as the host-side
-// ((x.float() * mul) @ W).to(dtype) of upstream forward.py:279-286 and
-// backward.py:546-547, up to the order of the DH-term sum. x is read from a
-// staged shared tile [h][q][DHP] (the swizzled 16-bit layout the kernels
-// stage Q and dO in); W comes from global memory (it is tiny and stays in
-// L1). The result goes to a swizzled shared tile [q][16][CP] (head rows >= NH,
-// channels >= C and rows >= nvalid are written as zeros) and, if gdst is
-// given, to global memory in the [rows, H, C] layout, rows i0 + q of event ev.
-template <typename T, int DH, int C, int CP, int RBD>
-__device__ __forceinline__ void project_staged(const FstProblem& p, const unsigned char* xs,
-                                               int rows_per_head, float mul, const EventSpan& ev,
-                                               int i0, int nvalid, int nrows, int h0, int NH,
-                                               unsigned char* tile, T* __restrict__ gdst) {
+// Projection of one head's block of BM rows through the encoder weight on the
+// tensor cores, the arithmetic of the host-side ((x.float() * mul) @ W).to(T)
+// of upstream forward.py:279-286 and backward.py:546-547:
+//   out[q][c] = [ mul * sum_d x[q][d] W[d][c] ]
+// x comes from the staged swizzled tile of this head ([BM][DHP], 16-bit, as
+// the kernels stage Q and dO), W from the staged [DH][CP] tiles of its hi and
+// lo halves in T (W = W_hi + W_lo to ~16 significant bits; x is exact in T),
+// the products are accumulated in fp32 and rounded once to T. One warp per
+// head: rows q < nvalid go to gdst (rows i0 + q of event ev, head h), and, if
+// tile is given, all BM rows go to row (q * 16 + hl) of the swizzled
+// [BM][16][CP] tile the heads-on-M MMAs read.
+template <typename T, int DH, int C, int CP, int RBD, int BM>
+__device__ __forceinline__ void project_mma(uint32_t x_tile, uint32_t w_hi, uint32_t w_lo,
+                                            float mul, const EventSpan& ev, int i0, int nvalid,
+                                            int h, int hl, unsigned char* tile,
+                                            T* __restrict__ gdst) {
   using E = Elem<T>;
-  constexpr int RBC = CP * 2;
-  for (int idx = threadIdx.x; idx < nrows * 16 * (CP / 2); idx += blockDim.x) {
-    const int c2 = idx % (CP / 2), h = (idx / (CP / 2)) % 16, q = idx / (16 * (CP / 2));
-    uint32_t packed = 0u;
-    if (q < nvalid && h < NH && 2 * c2 < C) {
-      const unsigned char* xr = xs + h * rows_per_head * RBD;
-      float a0 = 0.f, a1 = 0.f;
+  constexpr int RG = BM / 16, KSD = DH / 16, NTC = C / 8, RBC = CP * 2;
+  static_assert(NTC % 2 == 0, "n-tiles come in pairs");
+  const int lane = threadIdx.x & 31, m4 = lane & 3, r8 = lane >> 2, mi = lane >> 3;
+  float acc[RG][NTC][4];
 #pragma unroll
-      for (int ch = 0; ch < DH / 8; ++ch) {
-        const uint4 raw = *(const uint4*)(xr + swz<RBD>(q, ch));
-        const uint32_t* w2 = (const uint32_t*)&raw;
+  for (int rg = 0; rg < RG; ++rg)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int d = ch * 8 + 2 * e;
-          const float x0 = E::lo(w2[e]) * mul, x1 = E::hi(w2[e]) * mul;
-          const float2 wa = *(const float2*)(p.weight + (int64_t)d * C + 2 * c2);
-          const float2 wb = *(const float2*)(p.weight + (int64_t)(d + 1) * C + 2 * c2);
-          a0 = fmaf(x0, wa.x, a0);
-          a1 = fmaf(x0, wa.y, a1);
-          a0 = fmaf(x1, wb.x, a0);
-          a1 = fmaf(x1, wb.y, a1);
-        }
-      }
-      packed = E::pack(a0, a1);
-      if (gdst) *(uint32_t*)(gdst + ev_off(ev, i0 + q, h0 + h, C) + 2 * c2) = packed;
+    for (int nc = 0; nc < NTC; ++nc)
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[rg][nc][i] = 0.f;
+#pragma unroll
+  for (int ks = 0; ks < KSD; ++ks) {
+    // W B-fragments (k = d, n = c) from the [d][c] tiles by transposed loads.
+    uint32_t bh[NTC][2], bl[NTC][2];
+#pragma unroll
+    for (int np = 0; np < NTC / 2; ++np) {
+      const uint32_t off = swz<RBC>(ks * 16 + (mi & 1) * 8 + (lane & 7), 2 * np + (mi >> 1));
+      uint32_t r[4];
+      ldsm_x4_t(w_hi + off, r);
+      bh[2 * np][0] = r[0];
+      bh[2 * np][1] = r[1];
+      bh[2 * np + 1][0] = r[2];
+      bh[2 * np + 1][1] = r[3];
+      ldsm_x4_t(w_lo + off, r);
+      bl[2 * np][0] = r[0];
+      bl[2 * np][1] = r[1];
+      bl[2 * np + 1][0] = r[2];
+      bl[2 * np + 1][1] = r[3];
     }
-    if (tile) *(uint32_t*)(tile + swz<RBC>(q * 16 + h, c2 / 4) + (c2 % 4) * 4) = packed;
+#pragma unroll
+    for (int rg = 0; rg < RG; ++rg) {
+      uint32_t xa[4];
+      ldsm_x4(x_tile + swz<RBD>(rg * 16 + (mi & 1) * 8 + (lane & 7), 2 * ks + (mi >> 1)), xa);
+#pragma unroll
+      for (int nc = 0; nc < NTC; ++nc) {
+        mma16816<T>(acc[rg][nc], xa, bh[nc]);
+        mma16816<T>(acc[rg][nc], xa, bl[nc]);
+      }
+    }
   }
+#pragma unroll
+  for (int rg = 0; rg < RG; ++rg)
+#pragma unroll
+    for (int rh = 0; rh < 2; ++rh) {
+      const int q = rg * 16 + r8 + 8 * rh;
+      T* grow = (gdst != nullptr && q < nvalid) ? gdst + ev_off(ev, i0 + q, h, C) : nullptr;
+#pragma unroll
+      for (int nc = 0; nc < NTC; ++nc) {
+        const int c = nc * 8 + 2 * m4;
+        const uint32_t v = E::pack(acc[rg][nc][2 * rh] * mul, acc[rg][nc][2 * rh + 1] * mul);
+        if (grow) *(uint32_t*)(grow + c) = v;
+        if (tile) *(uint32_t*)(tile + swz<RBC>(q * 16 + hl, nc) + m4 * 4) = v;
+      }
+    }
 }
 
 // Multiply a staged [h][q][DHP] 16-bit tile by `mul` in place, rounding once.

@@ -197,10 +197,14 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       *(uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c)) = v;
     }
     if (attn && gu == nullptr) {
-      // u = (q * scale) W computed here, in fp32, from the staged raw q.
-      __syncthreads();
-      project_staged<T, DH, C, S::CP, S::RBD>(p, smem + S::OFF_Q, S::BM, p.scale, ev, q0,
-                                              nvalid_q, S::BM, h0, NH, smem + S::OFF_U, nullptr);
+      // u is projected by the head warps below; the tile's head rows past the
+      // CTA's heads (the heads-on-M MMA reads 16) are zero.
+      constexpr int UCH = S::CP / 8;
+      const int zrows = 16 - NH;
+      for (int idx = threadIdx.x; idx < S::BM * zrows * UCH; idx += nthreads) {
+        const int c = idx % UCH, h = NH + (idx / UCH) % zrows, q = idx / (UCH * zrows);
+        *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = make_uint4(0, 0, 0, 0);
+      }
     } else {
       constexpr int UCH = S::CP / 8;
       for (int idx = threadIdx.x; idx < S::BM * 16 * UCH; idx += nthreads) {
@@ -211,12 +215,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         *(uint4*)(smem + S::OFF_U + swz<S::RBC>(q * 16 + h, c)) = v;
       }
     }
-    // W^T operand of the epilogue, split into hi + lo halves of the 16-bit type
-    // so that (A'/l) W^T keeps W at ~fp32 accuracy.
+    // W as [d][c], split into hi + lo halves of the 16-bit type so that the
+    // projection u = (q * scale) W and the epilogue's (A'/l) W^T keep W at
+    // ~fp32 accuracy.
     for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
       const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
       float w0 = 0.f, w1 = 0.f;
-      if (act && 2 * c2 < C) {
+      if ((attn || act) && 2 * c2 < C) {
         w0 = p.weight[(int64_t)d * C + 2 * c2];
         w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
       }
@@ -231,6 +236,11 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
     }
   }
+  __syncthreads();
+  if (attn && gu == nullptr && warp < NH)  // u = (q * scale) W, one head per warp
+    project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sQ + warp * S::BM * S::RBD, sW,
+                                                sW + DH * S::RBC, p.scale, ev, q0, nvalid_q,
+                                                h0 + warp, warp, smem + S::OFF_U, nullptr);
   __syncthreads();
   scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();

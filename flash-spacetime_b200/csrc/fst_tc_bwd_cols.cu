@@ -199,14 +199,31 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       ck[nt].z = fKC[j * 4 + 2];
       ck[nt].t = fKC[j * 4 + 3];
     }
+    // Bias-tile addressing of this lane's keys j = nt*8 + 2 m4 + r (bias_word
+    // split into its per-lane and per-query parts): byte offset of head r8's
+    // row of key j, and the key's swizzle group.
+    uint32_t krow[2][2];
+    int kgrp[2][2];
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+      for (int r = 0; r < 2; ++r) {
+        const int j = nt * 8 + 2 * m4 + r;
+        krow[nt][r] = (r8 * S::HS + j * S::JS) * 4;
+        kgrp[nt][r] = ((j >> 1) & 3) | ((j & 1) << 2);
+      }
     const uint32_t ring = sm + S::OFF_ER + e * 2 * S::SZ_ER;
     const float* __restrict__ fbase = p.feats + ev.row0 * p.feat_stride;
     auto load_ring = [&](int n) {
       if (n < nchunks) {
         const uint32_t st = ring + (n & 1) * S::SZ_ER;
         constexpr int CC = C / 8;  // 16-byte chunks per (q, h) row
-        for (int idx = lane; idx < S::QPE * NH * CC; idx += 32) {
-          const int c = idx % CC, h = (idx / CC) % NH, t = idx / (CC * NH);
+        constexpr int NIT = (S::QPE * S::HP * CC + 31) / 32;
+#pragma unroll
+        for (int it = 0; it < NIT; ++it) {
+          const int idx = it * 32 + lane;
+          const int c = idx % CC, h = (idx / CC) % S::HP, t = idx / (CC * S::HP);
+          if (t >= S::QPE || h >= NH) continue;
           const int i = n * S::BQ + e * S::QPE + t;
           const uint32_t off = swz<S::RBC>(t * S::HP + h, c);
           if (i < ev.len) {
@@ -306,10 +323,10 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
           const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS;
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
-            const int j = nt * 8 + 2 * m4 + r;
-            const int w = bias_word(j, qq, S::JS);
-            if (r8 < NH) sts_v2(base + (r8 * S::HS + w) * 4, du[r], dw[r]);
-            if (r8 + 8 < NH) sts_v2(base + ((r8 + 8) * S::HS + w) * 4, du[2 + r], dw[2 + r]);
+            const uint32_t a0 =
+                base + krow[nt][r] + 16 * ((qq >> 1) ^ kgrp[nt][r]) + 8 * (qq & 1);
+            if (r8 < NH) sts_v2(a0, du[r], dw[r]);
+            if (r8 + 8 < NH) sts_v2(a0 + 8 * S::HS * 4, du[2 + r], dw[2 + r]);
           }
         }
       }
@@ -435,29 +452,29 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     }
     if (n + 2 < nchunks) named_arrive(cb_bias_empty(s), NBAR);
 
-    // P^T and dS^T; queries past the event (last chunk) get P = 0.
+    // P^T and dS^T; queries past the event (last chunk only) get P = dS = 0.
     uint32_t pt[4], dt[4];
-    float amax[2][2] = {{0.f, 0.f}, {0.f, 0.f}};  // [nt][column pair member]
-    const bool qtail = i0 + S::BQ > ev.len;  // queries past the event: last chunk only
 #pragma unroll
     for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int qi = nt * 8 + 2 * m4 + c;
         const float l2 = stat[qi], dl = stat[S::BQ + qi];
-        const bool dead = qtail && i0 + qi >= ev.len;
 #pragma unroll
         for (int hi = 0; hi < 2; ++hi) {
           const int i = 2 * hi + c;
-          float pv = ex2(fmaf(sc[nt][i], kLog2e, -l2));
-          if (dead) pv = 0.f;
-          const float ds = pv * (dp[nt][i] - dl);
+          const float pv = ex2(fmaf(sc[nt][i], kLog2e, -l2));
+          dp[nt][i] = pv * (dp[nt][i] - dl);
           sc[nt][i] = pv;
-          dp[nt][i] = ds;
-          if (hi == 0 ? (r8 < nvalid_k) : (r8 + 8 < nvalid_k))
-            amax[nt][c] = fmaxf(amax[nt][c], fabsf(ds));
         }
       }
+    if (i0 + S::BQ > ev.len) {
+#pragma unroll
+      for (int nt = 0; nt < 2; ++nt)
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          if (i0 + nt * 8 + 2 * m4 + (i & 1) >= ev.len) sc[nt][i] = dp[nt][i] = 0.f;
+    }
     pt[0] = E::pack(sc[0][0], sc[0][1]);
     pt[1] = E::pack(sc[0][2], sc[0][3]);
     pt[2] = E::pack(sc[1][0], sc[1][1]);
@@ -473,7 +490,9 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          float v = amax[nt][c];
+          float v = 0.f;
+          if (r8 < nvalid_k) v = fabsf(dp[nt][c]);
+          if (r8 + 8 < nvalid_k) v = fmaxf(v, fabsf(dp[nt][2 + c]));
           v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 4));
           v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 8));
           v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, 16));

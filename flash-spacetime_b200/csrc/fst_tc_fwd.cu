@@ -45,6 +45,9 @@ namespace fst {
 namespace tc {
 
 constexpr int kHeadsPerCta = 12;
+// A row's reference max moves only when a chunk exceeds it by more than this
+// (log2 units), so the P values the MMAs see are at most 2^kLazyMax.
+constexpr float kLazyMax = 8.f;
 
 template <int DH, int C>
 struct FwdShape {
@@ -100,7 +103,8 @@ struct FwdShape {
   static constexpr int OFF_C = OFF_V + 2 * SZ_KV;             // key coords [NE][2][BN][4]
   static constexpr int OFF_QC = OFF_C + NE * 2 * BN * 16;     // query coords [BM][4]
   static constexpr int OFF_L = OFF_QC + BM * 16;              // row sums [BM][HP]
-  static constexpr int SMEM = OFF_L + BM * HP * 4;
+  static constexpr int OFF_F = OFF_L + BM * HP * 4;           // rescale flags [2][16] int
+  static constexpr int SMEM = OFF_F + 2 * 16 * 4;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -273,6 +277,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   __syncthreads();  // the staging tiles are dead; the exchange tiles take their place
   for (int idx = threadIdx.x; idx < 2 * S::SZ_P / 4; idx += nthreads)
     ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+  if (threadIdx.x < 32) ((int*)(smem + S::OFF_F))[threadIdx.x] = 0;
   __syncthreads();
 
   if (idle) {
@@ -333,8 +338,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     // embedding of chunk n+1 instead of following it.
     using EFrag = uint32_t[S::QPE][2][S::KSC][2];  // E B-fragments (k = channel, n = key)
     // Embedding of chunk n into eb and (attn) its logit bias into bias stage n & 1.
-    auto produce = [&](int n, EFrag& eb) {
-      const int s = n & 1;
+    auto produce = [&](int n, int s, EFrag& eb) {
       cp_async_wait<1>();
       __syncwarp();
       // x for (query qx_row, key nt*8 + r8).
@@ -394,15 +398,31 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       if (attn) named_arrive(bar_bias_full(s), NBAR);
     };
     // A'_q += P_q E_q for chunk n, after the online-softmax rescale.
-    auto consume = [&](int n, const EFrag& eb) {
-      const int s = n & 1;
+    auto consume = [&](int n, int s, const EFrag& eb) {
       named_sync(bar_p_full(s), NBAR);
+      // Did any head move a reference max this chunk? Otherwise every
+      // rescale factor is exactly 1 and A' is left as it is.
+      const int4* fl = (const int4*)(smem + S::OFF_F + s * 64);
+      const int4 f0 = fl[0], f1 = fl[1], f2 = fl[2];
+      const bool resc = (f0.x | f0.y | f0.z | f0.w | f1.x | f1.y | f1.z | f1.w | f2.x | f2.y |
+                         f2.z | f2.w) != 0;
 #pragma unroll
       for (int t = 0; t < S::QPE; ++t) {
         const int q = qe + t;
-        const float* alph = (const float*)(smem + S::OFF_A + (s * S::BM + q) * S::HP * 4);
-        const float a0 = r8 < NH ? alph[r8] : 1.f;
-        const float a1 = r8 + 8 < NH ? alph[r8 + 8] : 1.f;
+        if (resc) {
+          // Heads whose warp moved no reference left their factors unwritten: 1.
+          const float* alph = (const float*)(smem + S::OFF_A + (s * S::BM + q) * S::HP * 4);
+          const int* flg = (const int*)(smem + S::OFF_F + s * 64);
+          const float a0 = (r8 < NH && flg[r8]) ? alph[r8] : 1.f;
+          const float a1 = (r8 + 8 < NH && flg[r8 + 8]) ? alph[r8 + 8] : 1.f;
+#pragma unroll
+          for (int nc = 0; nc < S::NTC; ++nc) {
+            acc[t][nc][0] *= a0;
+            acc[t][nc][1] *= a0;
+            acc[t][nc][2] *= a1;
+            acc[t][nc][3] *= a1;
+          }
+        }
         uint32_t pa[4];
         {
           const int mi = lane >> 3;
@@ -411,10 +431,6 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         }
 #pragma unroll
         for (int nc = 0; nc < S::NTC; ++nc) {
-          acc[t][nc][0] *= a0;
-          acc[t][nc][1] *= a0;
-          acc[t][nc][2] *= a1;
-          acc[t][nc][3] *= a1;
           // E^T B-fragment (k = key, n = channel) by transposing the 8x8
           // blocks of the (k = channel, n = key) fragment in registers.
           uint32_t bt[2];
@@ -429,19 +445,22 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     if (attn || act) {
       if constexpr (S::AHEAD) {
         EFrag eb0, eb1;
-        produce(0, eb0);
+        produce(0, 0, eb0);
         for (int n = 0; n < nchunks; n += 2) {
-          if (n + 1 < nchunks) produce(n + 1, eb1);
-          if (act) consume(n, eb0);
+          if (n + 1 < nchunks) produce(n + 1, 1, eb1);
+          if (act) consume(n, 0, eb0);
           if (n + 1 >= nchunks) break;
-          if (n + 2 < nchunks) produce(n + 2, eb0);
-          if (act) consume(n + 1, eb1);
+          if (n + 2 < nchunks) produce(n + 2, 0, eb0);
+          if (act) consume(n + 1, 1, eb1);
         }
       } else {
         EFrag eb0;
-        for (int n = 0; n < nchunks; ++n) {
-          produce(n, eb0);
-          if (act) consume(n, eb0);
+        for (int n = 0; n < nchunks; n += 2) {
+          produce(n, 0, eb0);
+          if (act) consume(n, 0, eb0);
+          if (n + 1 >= nchunks) break;
+          produce(n + 1, 1, eb0);
+          if (act) consume(n + 1, 1, eb0);
         }
       }
     }
@@ -538,8 +557,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       lrun[rg][0] = lrun[rg][1] = 0.f;
     }
 
-    for (int n = 0; n < nchunks; ++n) {
-      const int s = n & 1;
+    // One key chunk; s = n & 1 is passed as a literal so that every stage
+    // offset folds into the shared-memory instructions.
+    auto step = [&](int n, int s) {
       const int j0 = n * S::BN;
       cp_async_wait<1>();
       __syncwarp();
@@ -622,11 +642,16 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
                            fmaxf(sc[rg][1][2 * rh], sc[rg][1][2 * rh + 1])) * kLog2e;
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
           mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-          mnew[rg][rh] = fmaxf(mrun[rg][rh], mx);
-          grew |= mnew[rg][rh] > mrun[rg][rh];
+          // The reference max of a row moves only when the chunk's max
+          // exceeds it by more than kLazyMax (log2 units), so P <= 2^kLazyMax;
+          // the final 1/l and the LSE use the same reference, so the result
+          // does not depend on when it moved.
+          const bool up = mx > mrun[rg][rh] + kLazyMax;
+          mnew[rg][rh] = up ? mx : mrun[rg][rh];
+          grew |= up;
         }
-      // The running max only moves now and then after the first chunks; when
-      // it moved for no row of the warp, every rescale factor is exactly 1.
+      // After the first chunk a reference rarely moves; when it moved for no
+      // row of the warp, every rescale factor is exactly 1.
       const bool rescale = __any_sync(0xffffffffu, grew);
 #pragma unroll
       for (int rg = 0; rg < S::RG; ++rg) {
@@ -644,7 +669,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
             }
           float al = 1.f;
           if (rescale) {
-            al = ex2(mrun[rg][rh] - muse);
+            al = mnew[rg][rh] != mrun[rg][rh] ? ex2(mrun[rg][rh] - muse) : 1.f;
 #pragma unroll
             for (int nd = 0; nd < S::NTD; ++nd) {
               o[rg][nd][2 * rh] *= al;
@@ -671,12 +696,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
           sts_u32(pbase + q * S::PQ * 4 + 16, pa[rg][2]);
           sts_u32(pbase + (q + 8) * S::PQ * 4, pa[rg][1]);
           sts_u32(pbase + (q + 8) * S::PQ * 4 + 16, pa[rg][3]);
-          if (m4 == 0) {
+          if (m4 == 0 && rescale) {
             float* al = (float*)(smem + S::OFF_A + s * S::BM * S::HP * 4);
             al[q * S::HP + hl] = alpha[rg][0];
             al[(q + 8) * S::HP + hl] = alpha[rg][1];
           }
         }
+        if (lane == 0) ((int*)(smem + S::OFF_F))[s * 16 + hl] = rescale ? 1 : 0;
         named_arrive(bar_p_full(s), NBAR);
       }
 
@@ -700,6 +726,10 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       }
       __syncwarp();
       load_kv(n + 2);  // stage s is free again
+    };
+    for (int n = 0; n < nchunks; n += 2) {
+      step(n, 0);
+      if (n + 1 < nchunks) step(n + 1, 1);
     }
 
     // Row sums over the quad, published for the E warps' A' normalisation.

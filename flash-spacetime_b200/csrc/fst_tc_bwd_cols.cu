@@ -39,6 +39,9 @@ struct ColShape {
   static constexpr int NE = BQ / QPE;
   static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;
   static constexpr int NWARPS = HP + NE;
+  // Loops unrolled by two chunks with literal ring stages where the
+  // registers allow it (the wide shapes would spill).
+  static constexpr bool LIT = C <= 16 && DH <= 32;
   static constexpr int KSD = DH / 16, NTD = DH / 8;
   static constexpr int KSC = C / 16;
   static constexpr int F = C / 2, FG = F / 8;
@@ -122,11 +125,14 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 
   if (k0 >= ev.len) {
     if (!p.packed) {
-      for (int idx = threadIdx.x; idx < NH * S::BK; idx += nthreads) {
-        const int h = h0 + idx / S::BK, j = k0 + idx % S::BK;
+      constexpr int CH = DH / 8;  // 16-byte chunks per row
+      for (int idx = threadIdx.x; idx < NH * S::BK * CH; idx += nthreads) {
+        const int c = idx % CH, r = idx / CH;
+        const int h = h0 + r / S::BK, j = k0 + r % S::BK;
         if (j >= p.max_len) continue;
-        const int64_t off = ev_off(ev, j, h, DH);
-        for (int d = 0; d < DH; ++d) gdk[off + d] = gdv[off + d] = from_f<T>(0.f);
+        const int64_t off = ev_off(ev, j, h, DH) + c * 8;
+        *(uint4*)(gdk + off) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(gdv + off) = make_uint4(0, 0, 0, 0);
       }
     }
     return;
@@ -250,8 +256,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     load_ring(0);
     load_ring(1);
 
-    for (int n = 0; n < nchunks; ++n) {
-      const int s = n & 1;
+    // One query chunk; the stage s = n & 1 is passed as a literal.
+    auto estep = [&](int n, int s) {
       cp_async_wait<1>();
       __syncwarp();
       const uint32_t st = ring + s * S::SZ_ER;
@@ -331,6 +337,14 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
         }
       }
       named_arrive(cb_bias_full(s), NBAR);
+    };
+    if constexpr (S::LIT) {
+      for (int n = 0; n < nchunks; n += 2) {
+        estep(n, 0);
+        if (n + 1 < nchunks) estep(n + 1, 1);
+      }
+    } else {
+      for (int n = 0; n < nchunks; ++n) estep(n, n & 1);
     }
     return;
   }
@@ -394,8 +408,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
     for (int i = 0; i < 4; ++i) dk[nd][i] = dv[nd][i] = 0.f;
 
-  for (int n = 0; n < nchunks; ++n) {
-    const int s = n & 1;
+  // One query chunk; the stage s = n & 1 is passed as a literal.
+  auto step = [&](int n, int s) {
     const int i0 = n * S::BQ;
     cp_async_wait<1>();
     __syncwarp();
@@ -524,6 +538,14 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     }
     __syncwarp();
     load_ring(n + 2);
+  };
+  if constexpr (S::LIT) {
+    for (int n = 0; n < nchunks; n += 2) {
+      step(n, 0);
+      if (n + 1 < nchunks) step(n + 1, 1);
+    }
+  } else {
+    for (int n = 0; n < nchunks; ++n) step(n, n & 1);
   }
 
 #pragma unroll

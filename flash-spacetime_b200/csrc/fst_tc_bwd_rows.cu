@@ -47,6 +47,9 @@ struct RowShape {
   // A-fragments are then re-read from a resident staged tile each chunk
   // instead of being held in registers.
   static constexpr bool AHEAD = C <= 16 && DH <= 32;
+  // Loops unrolled by two chunks with literal ring stages where the
+  // registers allow it (the wide shapes would spill).
+  static constexpr bool LIT = AHEAD;
   static constexpr int NWARPS = HP + NE;
   static constexpr int KSD = DH / 16, NTD = DH / 8;
   static constexpr int KSC = C / 16, NTC = C / 8;
@@ -153,14 +156,17 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     for (int i = threadIdx.x; i < DH * C; i += nthreads) dwp[i] = 0.f;
     for (int i = threadIdx.x; i < DH; i += nthreads) dbp[i] = 0.f;
     if (!p.packed) {
-      for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
-        const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
+      constexpr int CH = DH / 8;  // 16-byte chunks per row
+      for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
+        const int c = idx % CH, r = idx / CH;
+        const int h = h0 + r / S::BM, q = q0 + r % S::BM;
         if (q >= p.max_len) continue;
-        T* o = gdq + ev_off(ev, q, h, DH);
-        for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
-        const int64_t so = ev_off(ev, q, h, 1);
-        a.delta[so] = 0.f;
-        a.sigma[so] = 0.f;
+        *(uint4*)(gdq + ev_off(ev, q, h, DH) + c * 8) = make_uint4(0, 0, 0, 0);
+        if (c == 0) {
+          const int64_t so = ev_off(ev, q, h, 1);
+          a.delta[so] = 0.f;
+          a.sigma[so] = 0.f;
+        }
       }
     }
     return;
@@ -364,8 +370,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     // so the head warps' work on chunk n overlaps the embedding of chunk n+1.
     using EFrag = uint32_t[S::QPE][2][S::KSC][2];  // E B-fragments (k = channel, n = key)
     // Embedding of chunk n into eb and its (u.E, w~.E) bias into stage n & 1.
-    auto produce = [&](int n, EFrag& eb) {
-      const int s = n & 1;
+    auto produce = [&](int n, int s, EFrag& eb) {
       cp_async_wait<1>();
       __syncwarp();
       float xl[2];
@@ -439,8 +444,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       named_arrive(rb_bias_full(s), NBAR);
     };
     // H' += [P dP'] E and G += [P] E for chunk n.
-    auto consume = [&](int n, const EFrag& eb) {
-      const int s = n & 1;
+    auto consume = [&](int n, int s, const EFrag& eb) {
       named_sync(rb_p_full(s), NBAR);
 #pragma unroll
       for (int t = 0; t < S::QPE; ++t) {
@@ -467,19 +471,19 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
     if constexpr (S::AHEAD) {
       EFrag eb0, eb1;
-      produce(0, eb0);
+      produce(0, 0, eb0);
       for (int n = 0; n < nchunks; n += 2) {
-        if (n + 1 < nchunks) produce(n + 1, eb1);
-        consume(n, eb0);
+        if (n + 1 < nchunks) produce(n + 1, 1, eb1);
+        consume(n, 0, eb0);
         if (n + 1 >= nchunks) break;
-        if (n + 2 < nchunks) produce(n + 2, eb0);
-        consume(n + 1, eb1);
+        if (n + 2 < nchunks) produce(n + 2, 0, eb0);
+        consume(n + 1, 1, eb1);
       }
     } else {
       EFrag eb0;
       for (int n = 0; n < nchunks; ++n) {
-        produce(n, eb0);
-        consume(n, eb0);
+        produce(n, n & 1, eb0);
+        consume(n, n & 1, eb0);
       }
     }
 
@@ -602,8 +606,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     float pacc[4] = {0.f, 0.f, 0.f, 0.f}, aacc[4] = {0.f, 0.f, 0.f, 0.f};
     const uint32_t ones[2] = {E::kOnes, E::kOnes};
 
-    for (int n = 0; n < nchunks; ++n) {
-      const int s = n & 1;
+    // One key chunk; the stage s = n & 1 is passed as a literal.
+    auto step = [&](int n, int s) {
       const int j0 = n * S::BN;
       cp_async_wait<1>();
       __syncwarp();
@@ -721,6 +725,14 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       }
       __syncwarp();
       load_kv(n + 2);
+    };
+    if constexpr (S::LIT) {
+      for (int n = 0; n < nchunks; n += 2) {
+        step(n, 0);
+        if (n + 1 < nchunks) step(n + 1, 1);
+      }
+    } else {
+      for (int n = 0; n < nchunks; ++n) step(n, n & 1);
     }
 
     // D' = a / p, sigma = a - D' p, dqp = X - D' Y (rows r8 and r8 + 8).

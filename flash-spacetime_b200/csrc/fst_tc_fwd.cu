@@ -59,6 +59,9 @@ struct FwdShape {
   // E warps run one chunk ahead (two E fragments live) where the registers
   // allow it without spilling.
   static constexpr bool AHEAD = C <= 16 && DH <= 32;
+  // Loops unrolled by two chunks with literal ring stages where the
+  // registers allow it (the wide shapes would spill).
+  static constexpr bool LIT = AHEAD;
   static constexpr int HP = kHeadsPerCta;
   static constexpr int NWARPS = HP + NE;                      // max warps per CTA
   static constexpr int KSD = DH / 16, NTD = DH / 8;
@@ -169,12 +172,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   // layout) get zeros; nothing else to do.
   if (q0 >= ev.len) {
     if (!p.packed) {
-      for (int idx = threadIdx.x; idx < NH * S::BM; idx += nthreads) {
-        const int h = h0 + idx / S::BM, q = q0 + idx % S::BM;
+      constexpr int CH = DH / 8;  // 16-byte chunks per row
+      for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
+        const int c = idx % CH, r = idx / CH;
+        const int h = h0 + r / S::BM, q = q0 + r % S::BM;
         if (q >= p.max_len) continue;
-        T* o = gout + ev_off(ev, q, h, DH);
-        for (int d = 0; d < DH; ++d) o[d] = from_f<T>(0.f);
-        a.lse[ev_off(ev, q, h, 1)] = 0.f;
+        *(uint4*)(gout + ev_off(ev, q, h, DH) + c * 8) = make_uint4(0, 0, 0, 0);
+        if (c == 0) a.lse[ev_off(ev, q, h, 1)] = 0.f;
       }
     }
     return;
@@ -455,12 +459,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         }
       } else {
         EFrag eb0;
-        for (int n = 0; n < nchunks; n += 2) {
-          produce(n, 0, eb0);
-          if (act) consume(n, 0, eb0);
-          if (n + 1 >= nchunks) break;
-          produce(n + 1, 1, eb0);
-          if (act) consume(n + 1, 1, eb0);
+        for (int n = 0; n < nchunks; ++n) {
+          produce(n, n & 1, eb0);
+          if (act) consume(n, n & 1, eb0);
         }
       }
     }
@@ -727,9 +728,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       __syncwarp();
       load_kv(n + 2);  // stage s is free again
     };
-    for (int n = 0; n < nchunks; n += 2) {
-      step(n, 0);
-      if (n + 1 < nchunks) step(n + 1, 1);
+    if constexpr (S::LIT) {
+      for (int n = 0; n < nchunks; n += 2) {
+        step(n, 0);
+        if (n + 1 < nchunks) step(n + 1, 1);
+      }
+    } else {
+      for (int n = 0; n < nchunks; ++n) step(n, n & 1);
     }
 
     // Row sums over the quad, published for the E warps' A' normalisation.

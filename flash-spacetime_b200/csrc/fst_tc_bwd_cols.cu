@@ -56,7 +56,7 @@ struct ColShape {
   static constexpr int JS = 32;
   static constexpr int HS = BK * JS + 8;
   static constexpr int SZ_BIAS = HP * HS * 4;                 // one stage
-  // head-warp ring stage: Q chunk, dO chunk [BQ][DHP] + lse2, delta [BQ]
+  // head-warp ring stage: Q chunk, dO chunk [BQ][DHP] + LSE, D [BQ]
   static constexpr int SZ_HR = 2 * BQ * RBD + 2 * BQ * 4;
   // E-warp ring stage: u and w~ rows [QPE][HP][CP] + query coords [QPE][4].
   // The MMA's head rows past the CTA's heads read a shared zero row instead.
@@ -376,16 +376,16 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
                        "r"(0));
         }
       }
-      if (lane < S::BQ) {
+      if (lane < S::BQ) {  // LSE (natural log) and D of the chunk's queries
         const int qi = n * S::BQ + lane;
-        float l2 = 0.f, dl = 0.f;
+        const uint32_t f = st + 2 * S::BQ * S::RBD + lane * 4;
         if (qi < ev.len) {
-          l2 = lse_h[qi * ev.rs1] * kLog2e;
-          dl = delta_h[qi * ev.rs1];
+          cp_async4(f, lse_h + qi * ev.rs1);
+          cp_async4(f + S::BQ * 4, delta_h + qi * ev.rs1);
+        } else {
+          asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(f), "r"(0));
+          asm volatile("st.shared.u32 [%0], %1;\n" ::"r"(f + S::BQ * 4), "r"(0));
         }
-        float* f = (float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
-        f[lane] = l2;
-        f[S::BQ + lane] = dl;
       }
     }
     cp_async_commit();
@@ -473,7 +473,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
         const int qi = nt * 8 + 2 * m4 + c;
-        const float l2 = stat[qi], dl = stat[S::BQ + qi];
+        const float l2 = stat[qi] * kLog2e, dl = stat[S::BQ + qi];
 #pragma unroll
         for (int hi = 0; hi < 2; ++hi) {
           const int i = 2 * hi + c;

@@ -40,7 +40,10 @@ namespace tc {
 template <int DH, int C>
 struct RowShape {
   static constexpr int BM = 16, BN = 16;
-  static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1);
+  // Queries per E warp: two (eight E warps) at C <= 32 -- the E warps carry
+  // the longer dependency chain per key chunk, so they get two warps per
+  // scheduler.
+  static constexpr int QPE = C <= 32 ? 2 : 1;
   static constexpr int NE = BM / QPE;
   static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;  // heads per CTA
   // E warps run one chunk ahead (two E fragments live). Their u / w~

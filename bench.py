@@ -55,6 +55,23 @@ def _peaks():
         return {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0, "src": "fallback"}
 
 
+def _traffic(workload: str):
+    """DRAM bytes per launch of fst_forward / fst_backward from the committed
+    ncu summary of this workload (profiles/dram_traffic_<workload>.txt), or {}."""
+    path = os.path.join(ROOT, "profiles", f"dram_traffic_{workload}.txt")
+    out = {}
+    try:
+        with open(path) as f:
+            for line in f:
+                line = line.strip()
+                if line and not line.startswith("#") and "=" in line:
+                    k, v = line.split("=", 1)
+                    out[k] = v
+    except OSError:
+        return {}
+    return out if out.get("workload") == workload else {}
+
+
 def _dist_setup():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -346,6 +363,8 @@ def run_ours(args):
     dom_ms = bwd_ms if dom == "fst_backward" else fwd_ms
     dom_flops = flops["bwd"] if dom == "fst_backward" else flops["fwd"]
     achieved = dom_flops / (dom_ms * 1e-3) / 1e12 if dom_ms > 0 else 0.0
+    tr = _traffic(args.workload) if args.coords == "raw" and world == 1 else {}
+    traffic = int(tr[dom]) if dom in tr else None
 
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
@@ -370,7 +389,8 @@ def run_ours(args):
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "peak_gib": peak_gib,
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                     "frac": achieved / peaks["bf16_tflops"], "traffic": None,
+                     "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
+                     "traffic_unit": "bytes per launch (ncu dram read + write)",
                      "peak_src": peaks["src"] + " burst bf16"},
         "cpu_baseline": cpu,
         "clocks": clk,

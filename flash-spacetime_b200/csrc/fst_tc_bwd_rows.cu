@@ -91,7 +91,16 @@ struct RowShape {
   static constexpr int OFF_UWR = OFF_ST + 3 * BM * HP * 4;  // resident u, w~ (AHEAD)
   static constexpr int OFF_U = AHEAD ? OFF_UWR : 0;
   static constexpr int OFF_WT = OFF_U + SZ_US;
-  static constexpr int SMEM = OFF_UWR + (AHEAD ? 2 * SZ_US : 0);
+  static constexpr int END_UW = OFF_UWR + (AHEAD ? 2 * SZ_US : 0);
+  // Fast prologue / epilogue (AHEAD shapes that fit): raw q and dO stay
+  // resident for the whole kernel (projections, dO fragments, dW partials),
+  // and every prologue copy is one batch of cp.async; `out` rows for the row
+  // offsets are staged in the union region next to the scaled Q.
+  static constexpr int OFF_QR = END_UW, OFF_DOR = OFF_QR + SZ_QS;
+  static constexpr int OFF_OS = SZ_QS;
+  static constexpr bool FASTPRO = AHEAD && OFF_DOR + SZ_QS <= 227 * 1024;
+  static constexpr int SMEM = FASTPRO ? OFF_DOR + SZ_QS : END_UW;
+  static_assert(!FASTPRO || 2 * SZ_QS <= OFF_P, "staged Q / out do not overlap the P tiles");
   static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
   static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
   static_assert(2 * HP * BM * RBD <= 4 * SZ_KV, "staged q, dO fit the K/V ring");
@@ -183,23 +192,47 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   float* fCoff = fLse + S::BM * S::HP;
   float* fDp = fCoff + S::BM * S::HP;
 
-  // ------------------------------- prologue -------------------------------
-  {
+  const int m4 = lane & 3, r8 = lane >> 2;
+  const bool idle = warp >= NH + NE;
+  uint32_t qa[S::KSD][4], da[S::KSD][4];  // head warps: Q (scaled) and dO, rows on M
+  uint32_t ua[S::QPE][S::KSC][4], wa[S::QPE][S::KSC][4];  // E warps: u_q, w~_q
+  if constexpr (S::FASTPRO) {
+    // --------------------- prologue (one round of copies) ---------------------
     constexpr int QCH = DH / 8;
+    const bool proj_u = attn && a.u == nullptr, proj_w = act && a.wt == nullptr;
     for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
-      uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
-      if (q < nvalid_q) {  // raw q (scaled in place after the projections)
-        const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
-        vq = *(const uint4*)(gq + go);
-        vd = *(const uint4*)(gdo + go);
-      }
       const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
-      *(uint4*)(smem + S::OFF_Q + off) = vq;
-      *(uint4*)(smem + S::OFF_DO + off) = vd;
+      if (q < nvalid_q) {
+        const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
+        cp_async16(sm + S::OFF_QR + off, gq + go);
+        cp_async16(sm + S::OFF_DOR + off, gdo + go);
+        if (gout) cp_async16(sm + S::OFF_OS + off, gout + go);
+      } else {
+        *(uint4*)(smem + S::OFF_QR + off) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(smem + S::OFF_DOR + off) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(smem + S::OFF_OS + off) = make_uint4(0, 0, 0, 0);
+      }
     }
-    // W as [d][c], split into hi + lo halves of the 16-bit type: operand of
-    // the projections below and of R = H W^T in the epilogue.
+    for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
+      const int q = idx / NH, h = idx % NH;
+      const uint32_t dst = smem_u32(fLse + q * S::HP + h);
+      if (q < nvalid_q)
+        cp_async4(dst, a.lse + ev_off(ev, q0 + q, h0 + h, 1));
+      else
+        fLse[q * S::HP + h] = 0.f;
+    }
+    for (int q = threadIdx.x; q < S::BM; q += nthreads) {
+      const uint32_t dst = smem_u32(fQC + q * 4);
+      if (q < nvalid_q)
+        cp_async16(dst, p.feats + (ev.row0 + q0 + q) * p.feat_stride);
+      else
+        *(float4*)(fQC + q * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
+    // While the copies are in flight: W as [d][c] split into hi + lo halves,
+    // the zero head rows of the projected tiles, the P tiles, and caller-given
+    // u / w~ (if any).
     for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
       const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
       float w0 = 0.f, w1 = 0.f;
@@ -213,21 +246,36 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       *(uint32_t*)(smem + S::OFF_W + off) = hi;
       *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
     }
-  }
-  __syncthreads();
-  // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b),
-  // dO from the staged tile and out with 16-byte loads (d in order).
-  for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
-    const int q = idx / NH, h = idx % NH;
-    float l2 = 0.f, c = 0.f;
-    if (q < nvalid_q) {
-      l2 = a.lse[ev_off(ev, q0 + q, h0 + h, 1)] * kLog2e;
-      if (gout) {
-        const T* orow = gout + ev_off(ev, q0 + q, h0 + h, DH);
-        const unsigned char* drow = smem + S::OFF_DO + h * S::BM * S::RBD;
+    {
+      constexpr int UCH = S::CP / 8;
+      const int zrows = 16 - NH;
+      for (int idx = threadIdx.x; idx < S::BM * zrows * UCH; idx += nthreads) {
+        const int c = idx % UCH, h = NH + (idx / UCH) % zrows, q = idx / (UCH * zrows);
+        const uint32_t off = swz<S::RBC>(q * 16 + h, c);
+        if (proj_u) *(uint4*)(smem + S::OFF_U + off) = make_uint4(0, 0, 0, 0);
+        if (proj_w) *(uint4*)(smem + S::OFF_WT + off) = make_uint4(0, 0, 0, 0);
+      }
+    }
+    for (int idx = threadIdx.x; idx < 4 * S::SZ_P / 4; idx += nthreads)
+      ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+    if (attn && !proj_u)
+      stage_rows<T, C, S::CP>((const T*)a.u, ev, q0, nvalid_q, S::BM, h0, NH, smem + S::OFF_U);
+    if (act && !proj_w)
+      stage_rows<T, C, S::CP>((const T*)a.wt, ev, q0, nvalid_q, S::BM, h0, NH,
+                              smem + S::OFF_WT);
+    cp_async_wait<0>();
+    __syncthreads();
+    // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b),
+    // d in order. Rows past the event were staged as zeros (c = 0, LSE 0).
+    for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
+      const int q = idx / NH, h = idx % NH;
+      float c = 0.f;
+      if (gout && q < nvalid_q) {
+        const unsigned char* orow = smem + S::OFF_OS + h * S::BM * S::RBD;
+        const unsigned char* drow = smem + S::OFF_DOR + h * S::BM * S::RBD;
 #pragma unroll
-        for (int ch = 0; ch < DH / 8; ++ch) {
-          const uint4 ov = *(const uint4*)(orow + ch * 8);
+        for (int ch = 0; ch < QCH; ++ch) {
+          const uint4 ov = *(const uint4*)(orow + swz<S::RBD>(q, ch));
           const uint4 dv = *(const uint4*)(drow + swz<S::RBD>(q, ch));
           const uint32_t* o2 = (const uint32_t*)&ov;
           const uint32_t* d2 = (const uint32_t*)&dv;
@@ -243,83 +291,181 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
           }
         }
       }
+      fLse[q * S::HP + h] *= kLog2e;
+      fCoff[q * S::HP + h] = c;
     }
-    fLse[q * S::HP + h] = l2;
-    fCoff[q * S::HP + h] = c;
-  }
-  // u = (q * scale) W and w~ = dO W from the staged raw rows (one head per
-  // warp, on the tensor cores), unless the caller passed them; they go to the
-  // workspace, where phase 2 below and the column kernel read them.
-  if (warp < NH) {
-    const uint32_t sW = sm + S::OFF_W, sWlo = sW + DH * S::RBC;
-    if (attn && a.u == nullptr)
-      project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_Q + warp * S::BM * S::RBD, sW,
-                                                  sWlo, p.scale, ev, q0, nvalid_q, h0 + warp,
-                                                  warp, nullptr, u_ws);
-    if (act && a.wt == nullptr)
-      project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_DO + warp * S::BM * S::RBD, sW,
-                                                  sWlo, 1.f, ev, q0, nvalid_q, h0 + warp, warp,
-                                                  nullptr, wt_ws);
-  }
-  __syncthreads();
-  scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
-  __syncthreads();
-  {
-    // qt of the valid rows to the workspace, for the column kernel.
-    constexpr int QCH = DH / 8;
-    for (int idx = threadIdx.x; idx < NH * nvalid_q * QCH; idx += nthreads) {
-      const int c = idx % QCH, q = (idx / QCH) % nvalid_q, h = idx / (QCH * nvalid_q);
-      *(uint4*)(qt_ws + ev_off(ev, q0 + q, h0 + h, DH) + c * 8) =
-          *(const uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c));
-    }
-  }
-  const int m4 = lane & 3, r8 = lane >> 2;
-  const bool idle = warp >= NH + NE;
-  uint32_t qa[S::KSD][4], da[S::KSD][4];  // head warps: Q (scaled) and dO, rows on M
-  uint32_t ua[S::QPE][S::KSC][4], wa[S::QPE][S::KSC][4];  // E warps: u_q, w~_q
-  if (warp < NH) {
+    // qt = [q * scale] into the union region (head-warp fragments), its valid
+    // rows to the workspace for the column kernel.
+    for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
+      const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
+      const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
+      uint4 v = *(const uint4*)(smem + S::OFF_QR + off);
+      uint32_t* w = (uint32_t*)&v;
 #pragma unroll
-    for (int ks = 0; ks < S::KSD; ++ks) {
-      const int mi = lane >> 3;
-      const int q = (mi & 1) * 8 + (lane & 7);
-      const uint32_t off = warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1));
-      ldsm_x4(sm + S::OFF_Q + off, qa[ks]);
-      ldsm_x4(sm + S::OFF_DO + off, da[ks]);
+      for (int k = 0; k < 4; ++k) w[k] = E::pack(E::lo(w[k]) * p.scale, E::hi(w[k]) * p.scale);
+      *(uint4*)(smem + S::OFF_Q + off) = v;
+      if (q < nvalid_q) *(uint4*)(qt_ws + ev_off(ev, q0 + q, h0 + h, DH) + c * 8) = v;
     }
-  }
-  __syncthreads();  // phase 2 of the staging reuses the Q / dO bytes
-  {
-    if (attn)
-      stage_rows<T, C, S::CP>(a.u ? (const T*)a.u : u_ws, ev, q0, nvalid_q, S::BM, h0, NH,
-                              smem + S::OFF_U);
-    if (act)
-      stage_rows<T, C, S::CP>(a.wt ? (const T*)a.wt : wt_ws, ev, q0, nvalid_q, S::BM, h0, NH,
-                              smem + S::OFF_WT);
-    for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
-      const int q = idx / 4, k = idx % 4;
-      fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
+    // u = (q * scale) W and w~ = dO W (one head per warp, tensor cores) into
+    // the resident tiles and the workspace (for the column kernel).
+    if (warp < NH) {
+      const uint32_t sW = sm + S::OFF_W, sWlo = sW + DH * S::RBC;
+      if (proj_u)
+        project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_QR + warp * S::BM * S::RBD, sW,
+                                                    sWlo, p.scale, ev, q0, nvalid_q, h0 + warp,
+                                                    warp, smem + S::OFF_U, u_ws);
+      if (proj_w)
+        project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_DOR + warp * S::BM * S::RBD, sW,
+                                                    sWlo, 1.f, ev, q0, nvalid_q, h0 + warp, warp,
+                                                    smem + S::OFF_WT, wt_ws);
     }
-  }
-  __syncthreads();
-  if (warp >= NH && !idle) {
-    const int qe = (warp - NH) * S::QPE;
+    __syncthreads();
+    if (warp < NH) {
 #pragma unroll
-    for (int t = 0; t < S::QPE; ++t)
-#pragma unroll
-      for (int ks = 0; ks < S::KSC; ++ks) {
+      for (int ks = 0; ks < S::KSD; ++ks) {
         const int mi = lane >> 3;
-        const int h = (mi & 1) * 8 + (lane & 7);
-        const uint32_t off = swz<S::RBC>((qe + t) * 16 + h, 2 * ks + (mi >> 1));
-        if (!S::AHEAD) {
-          ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
-          ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+        const int q = (mi & 1) * 8 + (lane & 7);
+        const uint32_t off = warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1));
+        ldsm_x4(sm + S::OFF_Q + off, qa[ks]);
+        ldsm_x4(sm + S::OFF_DOR + off, da[ks]);
+      }
+    }
+    __syncthreads();  // the loop's bias tiles reuse the scaled-Q bytes
+  } else {
+    // ------------------------------- prologue -------------------------------
+    {
+      constexpr int QCH = DH / 8;
+      for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
+        const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
+        uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
+        if (q < nvalid_q) {  // raw q (scaled in place after the projections)
+          const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
+          vq = *(const uint4*)(gq + go);
+          vd = *(const uint4*)(gdo + go);
+        }
+        const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
+        *(uint4*)(smem + S::OFF_Q + off) = vq;
+        *(uint4*)(smem + S::OFF_DO + off) = vd;
+      }
+      // W as [d][c], split into hi + lo halves of the 16-bit type: operand of
+      // the projections below and of R = H W^T in the epilogue.
+      for (int idx = threadIdx.x; idx < DH * (S::CP / 2); idx += nthreads) {
+        const int c2 = idx % (S::CP / 2), d = idx / (S::CP / 2);
+        float w0 = 0.f, w1 = 0.f;
+        if ((attn || act) && 2 * c2 < C) {
+          w0 = p.weight[(int64_t)d * C + 2 * c2];
+          w1 = p.weight[(int64_t)d * C + 2 * c2 + 1];
+        }
+        const uint32_t hi = E::pack(w0, w1);
+        const uint32_t lo = E::pack(w0 - E::lo(hi), w1 - E::hi(hi));
+        const uint32_t off = swz<S::RBC>(d, c2 / 4) + (c2 % 4) * 4;
+        *(uint32_t*)(smem + S::OFF_W + off) = hi;
+        *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
+      }
+    }
+    __syncthreads();
+    // Per (row, head): LSE in log2 units and the row offset c = dO.(out - [act] b),
+    // dO from the staged tile and out with 16-byte loads (d in order).
+    for (int idx = threadIdx.x; idx < S::BM * NH; idx += nthreads) {
+      const int q = idx / NH, h = idx % NH;
+      float l2 = 0.f, c = 0.f;
+      if (q < nvalid_q) {
+        l2 = a.lse[ev_off(ev, q0 + q, h0 + h, 1)] * kLog2e;
+        if (gout) {
+          const T* orow = gout + ev_off(ev, q0 + q, h0 + h, DH);
+          const unsigned char* drow = smem + S::OFF_DO + h * S::BM * S::RBD;
+#pragma unroll
+          for (int ch = 0; ch < DH / 8; ++ch) {
+            const uint4 ov = *(const uint4*)(orow + ch * 8);
+            const uint4 dv = *(const uint4*)(drow + swz<S::RBD>(q, ch));
+            const uint32_t* o2 = (const uint32_t*)&ov;
+            const uint32_t* d2 = (const uint32_t*)&dv;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+              float o0 = E::lo(o2[e]), o1 = E::hi(o2[e]);
+              if (act && p.bias) {
+                o0 -= p.bias[ch * 8 + 2 * e];
+                o1 -= p.bias[ch * 8 + 2 * e + 1];
+              }
+              c = fmaf(E::lo(d2[e]), o0, c);
+              c = fmaf(E::hi(d2[e]), o1, c);
+            }
+          }
         }
       }
+      fLse[q * S::HP + h] = l2;
+      fCoff[q * S::HP + h] = c;
+    }
+    // u = (q * scale) W and w~ = dO W from the staged raw rows (one head per
+    // warp, on the tensor cores), unless the caller passed them; they go to the
+    // workspace, where phase 2 below and the column kernel read them.
+    if (warp < NH) {
+      const uint32_t sW = sm + S::OFF_W, sWlo = sW + DH * S::RBC;
+      if (attn && a.u == nullptr)
+        project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_Q + warp * S::BM * S::RBD, sW,
+                                                    sWlo, p.scale, ev, q0, nvalid_q, h0 + warp,
+                                                    warp, nullptr, u_ws);
+      if (act && a.wt == nullptr)
+        project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sm + S::OFF_DO + warp * S::BM * S::RBD, sW,
+                                                    sWlo, 1.f, ev, q0, nvalid_q, h0 + warp, warp,
+                                                    nullptr, wt_ws);
+    }
+    __syncthreads();
+    scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
+    __syncthreads();
+    {
+      // qt of the valid rows to the workspace, for the column kernel.
+      constexpr int QCH = DH / 8;
+      for (int idx = threadIdx.x; idx < NH * nvalid_q * QCH; idx += nthreads) {
+        const int c = idx % QCH, q = (idx / QCH) % nvalid_q, h = idx / (QCH * nvalid_q);
+        *(uint4*)(qt_ws + ev_off(ev, q0 + q, h0 + h, DH) + c * 8) =
+            *(const uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c));
+      }
+    }
+    if (warp < NH) {
+#pragma unroll
+      for (int ks = 0; ks < S::KSD; ++ks) {
+        const int mi = lane >> 3;
+        const int q = (mi & 1) * 8 + (lane & 7);
+        const uint32_t off = warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1));
+        ldsm_x4(sm + S::OFF_Q + off, qa[ks]);
+        ldsm_x4(sm + S::OFF_DO + off, da[ks]);
+      }
+    }
+    __syncthreads();  // phase 2 of the staging reuses the Q / dO bytes
+    {
+      if (attn)
+        stage_rows<T, C, S::CP>(a.u ? (const T*)a.u : u_ws, ev, q0, nvalid_q, S::BM, h0, NH,
+                                smem + S::OFF_U);
+      if (act)
+        stage_rows<T, C, S::CP>(a.wt ? (const T*)a.wt : wt_ws, ev, q0, nvalid_q, S::BM, h0, NH,
+                                smem + S::OFF_WT);
+      for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
+        const int q = idx / 4, k = idx % 4;
+        fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
+      }
+    }
+    __syncthreads();
+    if (warp >= NH && !idle) {
+      const int qe = (warp - NH) * S::QPE;
+#pragma unroll
+      for (int t = 0; t < S::QPE; ++t)
+#pragma unroll
+        for (int ks = 0; ks < S::KSC; ++ks) {
+          const int mi = lane >> 3;
+          const int h = (mi & 1) * 8 + (lane & 7);
+          const uint32_t off = swz<S::RBC>((qe + t) * 16 + h, 2 * ks + (mi >> 1));
+          if (!S::AHEAD) {
+            ldsm_x4(sm + S::OFF_U + off, ua[t][ks]);
+            ldsm_x4(sm + S::OFF_WT + off, wa[t][ks]);
+          }
+        }
+    }
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < 4 * S::SZ_P / 4; idx += nthreads)
+      ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+    __syncthreads();
   }
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < 4 * S::SZ_P / 4; idx += nthreads)
-    ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
-  __syncthreads();
 
   if (idle) {
     // Surplus warps of a short head group: no role in the key loop, but they
@@ -787,11 +933,13 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     }
   }
   if (warp >= NH) __syncthreads();  // (B) from the E-warp and idle-warp side
-  __syncthreads();  // (C) head warps are done with R; the K/V ring is free
-  // Stage this CTA's raw q and dO as [head][row][DHP] swizzled tiles in the
-  // K/V ring (rows past the event are zero) for the dW / db partials.
-  const uint32_t sq = sm + S::OFF_K, sdo = sq + S::HP * S::BM * S::RBD;
-  {
+  // Raw q and dO as [head][row][DHP] swizzled tiles (rows past the event are
+  // zero) for the dW / db partials: resident since the prologue on the fast
+  // path; otherwise staged again into the K/V ring once R is consumed.
+  const uint32_t sq = S::FASTPRO ? sm + S::OFF_QR : sm + S::OFF_K;
+  const uint32_t sdo = S::FASTPRO ? sm + S::OFF_DOR : sq + S::HP * S::BM * S::RBD;
+  if constexpr (!S::FASTPRO) {
+    __syncthreads();  // (C) head warps are done with R; the K/V ring is free
     constexpr int CH = DH / 8;
     for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
       const int c = idx % CH, q = (idx / CH) % S::BM, hl = idx / (CH * S::BM);
@@ -805,8 +953,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       *(uint4*)(smem + (sq - sm) + so) = vq;
       *(uint4*)(smem + (sdo - sm) + so) = vd;
     }
+    __syncthreads();  // (D)
   }
-  __syncthreads();  // (D)
   // dW and db partials of this CTA (backward.py:607-622) on the tensor cores,
   // one (16 d x 8 c) output tile per warp, K running over (head, row) in a
   // fixed order:
@@ -819,7 +967,10 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     const int nwarps = nthreads >> 5;
     const int mi = lane >> 3;
     const uint32_t ones[2] = {E::kOnes, E::kOnes};
-    for (int tile = warp; tile < MT * NTW; tile += nwarps) {
+    // On the fast path the tiles go to the last warps (E and idle warps), which
+    // run them while the head warps write dq.
+    const int first = S::FASTPRO ? nwarps - 1 - warp : warp;
+    for (int tile = first; tile < MT * NTW; tile += nwarps) {
       const int mt = tile / NTW, nt = tile % NTW;
       const int c = nt * 8 + r8;  // this lane's B column
       // A = x^T (m = d, k = row) from the [row][d] tile by transposed loads.

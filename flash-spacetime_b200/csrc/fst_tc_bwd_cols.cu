@@ -145,25 +145,30 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 
   // ------------------------------ prologue ---------------------------------
   {
+    // One round of copies (cp.async) for K, V and the key coordinates.
     constexpr int CH = DH / 8;
     for (int idx = threadIdx.x; idx < NH * S::BK * CH; idx += nthreads) {
       const int c = idx % CH, j = (idx / CH) % S::BK, h = idx / (CH * S::BK);
-      uint4 vk = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+      const uint32_t off = h * S::BK * S::RBD + swz<S::RBD>(j, c);
       if (j < nvalid_k) {
         const int64_t go = ev_off(ev, k0 + j, h0 + h, DH) + c * 8;
-        vk = *(const uint4*)(gk + go);
-        vv = *(const uint4*)(gv + go);
+        cp_async16(sm + S::OFF_KS + off, gk + go);
+        cp_async16(sm + S::OFF_VS + off, gv + go);
+      } else {
+        *(uint4*)(smem + S::OFF_KS + off) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(smem + S::OFF_VS + off) = make_uint4(0, 0, 0, 0);
       }
-      const uint32_t off = h * S::BK * S::RBD + swz<S::RBD>(j, c);
-      *(uint4*)(smem + S::OFF_KS + off) = vk;
-      *(uint4*)(smem + S::OFF_VS + off) = vv;
     }
-    for (int idx = threadIdx.x; idx < S::BK * 4; idx += nthreads) {
-      const int j = idx / 4, k = idx % 4;
-      fKC[idx] = j < nvalid_k ? p.feats[(ev.row0 + k0 + j) * p.feat_stride + k] : 0.f;
+    for (int j = threadIdx.x; j < S::BK; j += nthreads) {
+      if (j < nvalid_k)
+        cp_async16(smem_u32(fKC + j * 4), p.feats + (ev.row0 + k0 + j) * p.feat_stride);
+      else
+        *(float4*)(fKC + j * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    cp_async_commit();
     for (int idx = threadIdx.x; idx < S::RBC / 4; idx += nthreads)
       ((uint32_t*)(smem + S::OFF_ZR))[idx] = 0u;
+    cp_async_wait<0>();
   }
   __syncthreads();
   const int m4 = lane & 3, r8 = lane >> 2;

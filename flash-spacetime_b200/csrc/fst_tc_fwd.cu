@@ -108,6 +108,9 @@ struct FwdShape {
   static constexpr int OFF_L = OFF_QC + BM * 16;              // row sums [BM][HP]
   static constexpr int OFF_F = OFF_L + BM * HP * 4;           // rescale flags [2][16] int
   static constexpr int SMEM = OFF_F + 2 * 16 * 4;
+  // Whether the P tiles lie clear of the staging bytes (then they are zeroed
+  // while Q and u are staged, saving a barrier).
+  static constexpr bool P_CLEAR = OFF_P >= SZ_STAGE;
   static_assert(SMEM <= 227 * 1024, "shared memory budget");
 };
 
@@ -194,16 +197,28 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   const uint32_t sL = sm + S::OFF_L;
   float* fQC = (float*)(smem + S::OFF_QC);
 
-  // ---------------- prologue: stage Q (scaled), u, W, query coords --------
+  // ---------------- prologue: stage Q, u, W, query coords ----------------
+  // One round of copies: raw q and the query coordinates by cp.async; while
+  // they are in flight, W (hi + lo), the u tile's zero rows (or a caller's u),
+  // the rescale flags and, where they lie clear of the staging bytes, the
+  // zeroed P tiles.
   {
     constexpr int QCH = DH / 8;  // 16-byte chunks per q row
     for (int idx = threadIdx.x; idx < NH * S::BM * QCH; idx += nthreads) {
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
-      uint4 v = make_uint4(0, 0, 0, 0);  // raw q; scaled in place below
+      const uint32_t off = S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c);
       if (q < nvalid_q)
-        v = *(const uint4*)(gq + ev_off(ev, q0 + q, h0 + h, DH) + c * 8);
-      *(uint4*)(smem + S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c)) = v;
+        cp_async16(sm + off, gq + ev_off(ev, q0 + q, h0 + h, DH) + c * 8);
+      else
+        *(uint4*)(smem + off) = make_uint4(0, 0, 0, 0);
     }
+    for (int q = threadIdx.x; q < S::BM; q += nthreads) {
+      if (q < nvalid_q)
+        cp_async16(smem_u32(fQC + q * 4), p.feats + (ev.row0 + q0 + q) * p.feat_stride);
+      else
+        *(float4*)(fQC + q * 4) = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    cp_async_commit();
     if (attn && gu == nullptr) {
       // u is projected by the head warps below; the tile's head rows past the
       // CTA's heads (the heads-on-M MMA reads 16) are zero.
@@ -239,18 +254,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       *(uint32_t*)(smem + S::OFF_W + off) = hi;
       *(uint32_t*)(smem + S::OFF_W + DH * S::RBC + off) = lo;
     }
-    for (int idx = threadIdx.x; idx < S::BM * 4; idx += nthreads) {
-      const int q = idx / 4, k = idx % 4;
-      fQC[idx] = q < nvalid_q ? p.feats[(ev.row0 + q0 + q) * p.feat_stride + k] : 0.f;
+    if constexpr (S::P_CLEAR) {
+      for (int idx = threadIdx.x; idx < 2 * S::SZ_P / 4; idx += nthreads)
+        ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
     }
+    if (threadIdx.x < 32) ((int*)(smem + S::OFF_F))[threadIdx.x] = 0;
+    cp_async_wait<0>();
   }
-  __syncthreads();
-  if (attn && gu == nullptr && warp < NH)  // u = (q * scale) W, one head per warp
-    project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sQ + warp * S::BM * S::RBD, sW,
-                                                sW + DH * S::RBC, p.scale, ev, q0, nvalid_q,
-                                                h0 + warp, warp, smem + S::OFF_U, nullptr);
-  __syncthreads();
-  scale_staged<T, DH, S::RBD>(smem + S::OFF_Q, NH, S::BM, p.scale);  // qt = [q * scale]
   __syncthreads();
 
   const int m4 = lane & 3, r8 = lane >> 2;
@@ -259,6 +269,12 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   uint32_t ua[S::QPE][S::KSC][4];  // E warps: u_q (heads on M)
   const bool idle = warp >= NH + NE;
   if (warp < NH) {
+    // u = (q * scale) W from the raw rows (one head per warp), then this
+    // head's qt = [q * scale] fragments, scaled in registers.
+    if (attn && gu == nullptr)
+      project_mma<T, DH, C, S::CP, S::RBD, S::BM>(sQ + warp * S::BM * S::RBD, sW,
+                                                  sW + DH * S::RBC, p.scale, ev, q0, nvalid_q,
+                                                  h0 + warp, warp, smem + S::OFF_U, nullptr);
 #pragma unroll
     for (int rg = 0; rg < S::RG; ++rg)
 #pragma unroll
@@ -266,8 +282,13 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         const int mi = lane >> 3;
         const int q = rg * 16 + (mi & 1) * 8 + (lane & 7);
         ldsm_x4(sQ + warp * S::BM * S::RBD + swz<S::RBD>(q, 2 * ks + (mi >> 1)), qa[rg][ks]);
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          qa[rg][ks][k] = E::pack(E::lo(qa[rg][ks][k]) * p.scale, E::hi(qa[rg][ks][k]) * p.scale);
       }
-  } else if (!idle) {
+  }
+  __syncthreads();  // u tile complete
+  if (warp >= NH && !idle) {
     const int qe = (warp - NH) * S::QPE;
 #pragma unroll
     for (int t = 0; t < S::QPE; ++t)
@@ -279,10 +300,11 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       }
   }
   __syncthreads();  // the staging tiles are dead; the exchange tiles take their place
-  for (int idx = threadIdx.x; idx < 2 * S::SZ_P / 4; idx += nthreads)
-    ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
-  if (threadIdx.x < 32) ((int*)(smem + S::OFF_F))[threadIdx.x] = 0;
-  __syncthreads();
+  if constexpr (!S::P_CLEAR) {
+    for (int idx = threadIdx.x; idx < 2 * S::SZ_P / 4; idx += nthreads)
+      ((uint32_t*)(smem + S::OFF_P))[idx] = 0u;
+    __syncthreads();
+  }
 
   if (idle) {
     __syncthreads();

@@ -299,47 +299,71 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       load_ring(n + 2);
 
       if (n >= 2) named_sync(cb_bias_empty(s), NBAR);
+      const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS;
+      // Queries are taken two at a time (when QPE is even), so that the (u.E,
+      // w~.E) pairs of queries 2k and 2k + 1 -- adjacent in the tile -- go out
+      // in one 16-byte store.
+      constexpr int TG = S::QPE % 2 == 0 ? 2 : 1;
 #pragma unroll
-      for (int t = 0; t < S::QPE; ++t) {
-        float sn[2][S::FG][2], cs[2][S::FG][2];
+      for (int tp = 0; tp < S::QPE; tp += TG) {
+        float du[TG][2][4], dw[TG][2][4];  // [query of the group][nt][fragment]
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+        for (int tt = 0; tt < TG; ++tt) {
+          const int t = tp + tt;
+          float sn[2][S::FG][2], cs[2][S::FG][2];
 #pragma unroll
-          for (int g = 0; g < S::FG; ++g)
+          for (int nt = 0; nt < 2; ++nt) {
+            const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
 #pragma unroll
-            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
-        }
-        const int qq = e * S::QPE + t;  // query index within the chunk
+            for (int g = 0; g < S::FG; ++g)
 #pragma unroll
-        for (int nt = 0; nt < 2; ++nt) {
-          uint32_t eb[S::KSC][2];
-#pragma unroll
-          for (int ks = 0; ks < S::KSC; ++ks)
-#pragma unroll
-            for (int hi = 0; hi < 2; ++hi) {
-              const int cb = 16 * ks + 8 * hi;
-              const int g = (cb % S::F) / 8;
-              const bool is_sin = cb < S::F;
-              eb[ks][hi] = E::pack(is_sin ? sn[nt][g][0] : cs[nt][g][0],
-                                   is_sin ? sn[nt][g][1] : cs[nt][g][1]);
-            }
-          float du[4] = {0.f, 0.f, 0.f, 0.f}, dw[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-          for (int ks = 0; ks < S::KSC; ++ks) {
-            if (attn) mma16816<T>(du, ua[t][ks], eb[ks]);
-            if (act) mma16816<T>(dw, wa[t][ks], eb[ks]);
+              for (int r = 0; r < 2; ++r)
+                sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
           }
-          // D[h][key]: h = r8 (+8), keys nt*8 + 2 m4 (+1). Tile [h][key][q].
-          const uint32_t base = sm + S::OFF_BIAS + s * S::SZ_BIAS;
+#pragma unroll
+          for (int nt = 0; nt < 2; ++nt) {
+            uint32_t eb[S::KSC][2];
+#pragma unroll
+            for (int ks = 0; ks < S::KSC; ++ks)
+#pragma unroll
+              for (int hi = 0; hi < 2; ++hi) {
+                const int cb = 16 * ks + 8 * hi;
+                const int g = (cb % S::F) / 8;
+                const bool is_sin = cb < S::F;
+                eb[ks][hi] = E::pack(is_sin ? sn[nt][g][0] : cs[nt][g][0],
+                                     is_sin ? sn[nt][g][1] : cs[nt][g][1]);
+              }
+#pragma unroll
+            for (int i = 0; i < 4; ++i) du[tt][nt][i] = dw[tt][nt][i] = 0.f;
+#pragma unroll
+            for (int ks = 0; ks < S::KSC; ++ks) {
+              if (attn) mma16816<T>(du[tt][nt], ua[t][ks], eb[ks]);
+              if (act) mma16816<T>(dw[tt][nt], wa[t][ks], eb[ks]);
+            }
+          }
+        }
+        // D[h][key]: h = r8 (+8), keys nt*8 + 2 m4 (+1). Tile [h][key][q].
+        const int qq = e * S::QPE + tp;  // query index within the chunk
+#pragma unroll
+        for (int nt = 0; nt < 2; ++nt)
 #pragma unroll
           for (int r = 0; r < 2; ++r) {
             const uint32_t a0 =
                 base + krow[nt][r] + 16 * ((qq >> 1) ^ kgrp[nt][r]) + 8 * (qq & 1);
-            if (r8 < NH) sts_v2(a0, du[r], dw[r]);
-            if (r8 + 8 < NH) sts_v2(a0 + 8 * S::HS * 4, du[2 + r], dw[2 + r]);
+            if constexpr (TG == 2) {
+              if (r8 < NH)
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(a0),
+                             "f"(du[0][nt][r]), "f"(dw[0][nt][r]), "f"(du[1][nt][r]),
+                             "f"(dw[1][nt][r]));
+              if (r8 + 8 < NH)
+                asm volatile("st.shared.v4.f32 [%0], {%1,%2,%3,%4};\n" ::"r"(a0 + 8 * S::HS * 4),
+                             "f"(du[0][nt][2 + r]), "f"(dw[0][nt][2 + r]), "f"(du[1][nt][2 + r]),
+                             "f"(dw[1][nt][2 + r]));
+            } else {
+              if (r8 < NH) sts_v2(a0, du[0][nt][r], dw[0][nt][r]);
+              if (r8 + 8 < NH) sts_v2(a0 + 8 * S::HS * 4, du[0][nt][2 + r], dw[0][nt][2 + r]);
+            }
           }
-        }
       }
       named_arrive(cb_bias_full(s), NBAR);
     };

@@ -421,6 +421,38 @@ def flash_spacetime_attention_varlen(
     )
 
 
+def flash_spacetime_attention_nested(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+) -> Tensor:
+    """The packed op on jagged NestedTensors (``layout=torch.jagged``).
+
+    q, k, v: ``[B, j, H, Dh]`` and feats ``[B, j, F]`` jagged along the event
+    axis with the same offsets -- the form whose values buffer and offsets
+    upstream's varlen entry point documents (forward.py:518-520). Returns a
+    jagged ``[B, j, H, Dh]`` with those offsets; gradients flow to the values
+    of q, k, v and to weight / bias as for the varlen op.
+    """
+    for name, t in (("q", q), ("k", k), ("v", v), ("feats", feats)):
+        if not (t.is_nested and t.layout == torch.jagged):
+            raise ValueError(f"{name} must be a jagged NestedTensor (layout=torch.jagged)")
+    offsets = q.offsets()
+    for name, t in (("k", k), ("v", v), ("feats", feats)):
+        if t.offsets() is not offsets and not torch.equal(t.offsets(), offsets):
+            raise ValueError(f"{name} must share q's offsets")
+    out = flash_spacetime_attention_varlen(
+        q.values(), k.values(), v.values(), feats.values(), weight, bias,
+        offsets.to(torch.int32), scale, use_attn_bias, use_activation_bias)
+    return torch.nested.nested_tensor_from_jagged(out, offsets)
+
+
 def flash_spacetime_forward(
     q: Tensor,
     k: Tensor,

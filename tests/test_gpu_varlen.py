@@ -209,3 +209,33 @@ def test_misaligned_views_match_aligned():
         results.append((out.detach().clone(), q.grad.clone(), w.grad.clone()))
     for a, b in zip(results[0], results[1]):
         assert torch.equal(a, b)
+
+
+def test_nested_tensor_adapter_matches_varlen():
+    # Jagged NestedTensors share the varlen op's values/offsets form: same
+    # values out, same gradients.
+    from flash_spacetime.ops import flash_spacetime_attention_nested
+
+    case = cs.packed_case([9, 130, 1, 57], 12, 32, 16, seed=123)
+    dtype = torch.bfloat16
+    cu = case["cu"].to(torch.int64)
+    go = torch.randn(case["q"].shape, generator=torch.Generator().manual_seed(9)).to("cuda", dtype)
+    res = []
+    for nested in (False, True):
+        q, k, v = (_to(case[x], dtype).requires_grad_(True) for x in ("q", "k", "v"))
+        feats = case["feats"].cuda()
+        w = _to(case["weight"], torch.float32).requires_grad_(True)
+        b = _to(case["bias"], torch.float32)
+        if nested:
+            offs = cu.cuda()
+            qn, kn, vn = (torch.nested.nested_tensor_from_jagged(t, offs) for t in (q, k, v))
+            fn = torch.nested.nested_tensor_from_jagged(feats, offs)
+            out = flash_spacetime_attention_nested(qn, kn, vn, fn, w, b)
+            assert out.is_nested and torch.equal(out.offsets(), offs)
+            out_v = out.values()
+        else:
+            out_v = flash_spacetime_attention_varlen(q, k, v, feats, w, b, case["cu"].cuda())
+        out_v.backward(go)
+        res.append((out_v.detach().clone(), q.grad.clone(), k.grad.clone(), w.grad.clone()))
+    for a, b in zip(res[0], res[1]):
+        assert torch.equal(a, b)

@@ -48,7 +48,10 @@ int check_problem(const FstProblem* p) {
                 p->channels);
   if (p->feat_stride < 4) return fail(FST_ERR_INVALID, "feat_stride must be >= 4");
   if (p->total_rows < 0) return fail(FST_ERR_INVALID, "negative total_rows");
-  if (p->packed) {
+  if (p->packed < 0 || p->packed > 2)
+    return fail(FST_ERR_INVALID, "unknown layout %d (0 padded BHLD, 1 packed, 2 padded BLHD)",
+                p->packed);
+  if (p->packed == 1) {
     if (!p->cu_seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "packed needs cu_seqlens");
   } else {
     if (!p->seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "padded needs seqlens");

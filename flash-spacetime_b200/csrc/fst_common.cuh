@@ -36,6 +36,15 @@ template <> __device__ __forceinline__ __half from_f<__half>(float x) {
   return __float2half_rn(x);
 }
 
+// Layouts (FstProblem::packed): 0 padded [B, H, L, *]; 1 packed (varlen)
+// [T, H, *] with cu_seqlens; 2 padded row-major [B, L, H, *] with seqlens --
+// the caller's [B, L, H*Dh] projections without a head split. Layouts 1 and 2
+// interleave heads within a row; only layout 1 uses the event tile list.
+__host__ __device__ __forceinline__ bool is_varlen(const FstProblem& p) { return p.packed == 1; }
+__host__ __device__ __forceinline__ bool rows_interleaved(const FstProblem& p) {
+  return p.packed != 0;
+}
+
 // Where one event lives. `row0` is the flat row of the event's first token in
 // the [rows] index space (padded: b*L, packed: cu[b]); `len` its valid length.
 // `base1`, `hs1` and `rs1` address its rows without any division: element
@@ -51,16 +60,19 @@ struct EventSpan {
 
 __device__ __forceinline__ EventSpan event_span(const FstProblem& p, int b) {
   EventSpan e;
-  if (p.packed) {
+  if (is_varlen(p)) {
     int s0 = p.cu_seqlens[b];
     e.row0 = s0;
     e.len = p.cu_seqlens[b + 1] - s0;
-    e.base1 = (int64_t)s0 * p.heads;
-    e.hs1 = 1;
-    e.rs1 = p.heads;
   } else {
     e.row0 = (int64_t)b * p.max_len;
     e.len = p.seqlens[b];
+  }
+  if (rows_interleaved(p)) {
+    e.base1 = e.row0 * p.heads;
+    e.hs1 = 1;
+    e.rs1 = p.heads;
+  } else {
     e.base1 = (int64_t)b * p.heads * p.max_len;
     e.hs1 = p.max_len;
     e.rs1 = 1;
@@ -87,7 +99,7 @@ __device__ __forceinline__ int packed_event_of(const int32_t* cu, int batch, int
 // Element offset of (row, head, 0) in a [*, H, D] (packed) or [B, H, L, D]
 // (padded) tensor, where `row` is a flat row index as in EventSpan.
 __device__ __forceinline__ int64_t vec_off(const FstProblem& p, int64_t row, int h, int dim) {
-  if (p.packed) return (row * p.heads + h) * (int64_t)dim;
+  if (rows_interleaved(p)) return (row * p.heads + h) * (int64_t)dim;
   int64_t b = row / p.max_len;
   int64_t i = row - b * p.max_len;
   return ((b * p.heads + h) * p.max_len + i) * (int64_t)dim;
@@ -96,7 +108,7 @@ __device__ __forceinline__ int64_t vec_off(const FstProblem& p, int64_t row, int
 // Element stride between consecutive rows of one event for a fixed head:
 // packed [T, H, D] rows are H*D apart, padded [B, H, L, D] rows D apart.
 __device__ __forceinline__ int row_stride(const FstProblem& p, int dim) {
-  return p.packed ? p.heads * dim : dim;
+  return rows_interleaved(p) ? p.heads * dim : dim;
 }
 
 // Offset of (row, head) in a per-row-per-head fp32 vector (LSE, D, sigma).

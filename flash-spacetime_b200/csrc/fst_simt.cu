@@ -39,7 +39,7 @@ __device__ __forceinline__ bool row_task(const FstProblem& p, int64_t gid, RowTa
   if (gid >= rows * p.heads) return false;
   t.row = gid / p.heads;
   t.h = (int)(gid - t.row * p.heads);
-  if (p.packed) {
+  if (is_varlen(p)) {
     t.b = packed_event_of(p.cu_seqlens, p.batch, t.row);
   } else {
     t.b = (int)(t.row / p.max_len);
@@ -388,7 +388,7 @@ __global__ void __launch_bounds__(256) dw_partial_kernel(FstBackwardArgs a, cons
     for (int64_t g = r0; g < r1; ++g) {
       const int64_t row = g / p.heads;
       const int h = (int)(g - row * p.heads);
-      if (!p.packed) {  // padding rows carry no gradient, whatever dout holds
+      if (!is_varlen(p)) {  // padding rows carry no gradient, whatever dout holds
         const int64_t b = row / p.max_len;
         if (row - b * p.max_len >= p.seqlens[b]) continue;
       }
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(256) dw_partial_kernel(FstBackwardArgs a, cons
     for (int64_t g = r0; g < r1; ++g) {
       const int64_t row = g / p.heads;
       const int h = (int)(g - row * p.heads);
-      if (!p.packed) {
+      if (!is_varlen(p)) {
         const int64_t b = row / p.max_len;
         if (row - b * p.max_len >= p.seqlens[b]) continue;
       }

@@ -95,7 +95,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   const FstProblem& p = a.prob;
 
   int b, kb;
-  if (!p.packed) {
+  if (!is_varlen(p)) {
     b = blockIdx.y;
     kb = blockIdx.x;
   } else {
@@ -124,7 +124,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   T* __restrict__ gdv = (T*)a.dv;
 
   if (k0 >= ev.len) {
-    if (!p.packed) {
+    if (!is_varlen(p)) {
       constexpr int CH = DH / 8;  // 16-byte chunks per row
       for (int idx = threadIdx.x; idx < NH * S::BK * CH; idx += nthreads) {
         const int c = idx % CH, r = idx / CH;
@@ -581,7 +581,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
   for (int rh = 0; rh < 2; ++rh) {
     const int j = r8 + 8 * rh;
     const bool valid = j < nvalid_k;
-    if (!valid && (p.packed || k0 + j >= p.max_len)) continue;
+    if (!valid && (is_varlen(p) || k0 + j >= p.max_len)) continue;
     const int64_t off = ev_off(ev, k0 + j, h, DH);
 #pragma unroll
     for (int nd = 0; nd < S::NTD; ++nd) {
@@ -611,7 +611,7 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
     const int per_group = (p.heads + groups - 1) / groups;
     const int threads = (per_group + S::NE) * 32;
     dim3 grid;
-    if (p.packed) {
+    if (is_varlen(p)) {
       // tile_start (16-row tiles) was built by the row kernel's launch.
       const int64_t upper = (p.total_rows + S::BK - 1) / S::BK + p.batch;
       grid = dim3((unsigned)upper, 1, groups);

@@ -123,7 +123,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   const FstProblem& p = a.prob;
 
   int b, qb;
-  if (!p.packed) {
+  if (!is_varlen(p)) {
     b = blockIdx.y;
     qb = blockIdx.x;
   } else {
@@ -144,7 +144,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     b = lo;
     qb = t - tile_start[b];
   }
-  const int64_t part = p.packed ? ((int64_t)blockIdx.z * gridDim.x + blockIdx.x)
+  const int64_t part = is_varlen(p) ? ((int64_t)blockIdx.z * gridDim.x + blockIdx.x)
                                 : (((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x +
                                    blockIdx.x);
   float* dwp = a.dw_partial + part * DH * C;
@@ -167,7 +167,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   if (q0 >= ev.len) {
     for (int i = threadIdx.x; i < DH * C; i += nthreads) dwp[i] = 0.f;
     for (int i = threadIdx.x; i < DH; i += nthreads) dbp[i] = 0.f;
-    if (!p.packed) {
+    if (!is_varlen(p)) {
       constexpr int CH = DH / 8;  // 16-byte chunks per row
       for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
         const int c = idx % CH, r = idx / CH;
@@ -907,7 +907,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     for (int rh = 0; rh < 2; ++rh) {
       const int q = r8 + 8 * rh;
       const bool valid = q < nvalid_q;
-      if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
+      if (!valid && (is_varlen(p) || q0 + q >= p.max_len)) continue;
       T* orow = gdq + ev_off(ev, q0 + q, h, DH);
 #pragma unroll
       for (int nd = 0; nd < S::NTD; ++nd) {
@@ -1033,7 +1033,7 @@ template <int DH, int C>
 static dim3 rows_grid(const FstProblem& p) {
   using S = RowShape<DH, C>;
   const int groups = (p.heads + S::HP - 1) / S::HP;
-  if (p.packed) {
+  if (is_varlen(p)) {
     const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
     return dim3((unsigned)upper, 1, groups);
   }
@@ -1055,7 +1055,7 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   const int groups = (int)grid.z;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;
-  if (p.packed) tile_prefix(p, S::BM, tile_start, st);
+  if (is_varlen(p)) tile_prefix(p, S::BM, tile_start, st);
   if (grid.x == 0 || grid.y == 0) return FST_OK;
   bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
                                                                  (T*)u_ws, (T*)wt_ws, (T*)qt_ws);

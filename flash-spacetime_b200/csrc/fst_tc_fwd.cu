@@ -125,7 +125,7 @@ __device__ __forceinline__ int bar_p_empty(int s) { return 7 + s; }
 // tiles whose exclusive prefix is tile_start[0..B].
 __device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_start, int& b,
                                          int& qb) {
-  if (!p.packed) {
+  if (!is_varlen(p)) {
     b = blockIdx.y;
     qb = blockIdx.x;
     return true;
@@ -174,7 +174,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   // A query block entirely past the event's end: padding rows (padded
   // layout) get zeros; nothing else to do.
   if (q0 >= ev.len) {
-    if (!p.packed) {
+    if (!is_varlen(p)) {
       constexpr int CH = DH / 8;  // 16-byte chunks per row
       for (int idx = threadIdx.x; idx < NH * S::BM * CH; idx += nthreads) {
         const int c = idx % CH, r = idx / CH;
@@ -780,7 +780,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       for (int rh = 0; rh < 2; ++rh) {
         const int q = rg * 16 + r8 + 8 * rh;
         const bool valid = q < nvalid_q;
-        if (!valid && (p.packed || q0 + q >= p.max_len)) continue;
+        if (!valid && (is_varlen(p) || q0 + q >= p.max_len)) continue;
         const float il = valid ? 1.f / lrun[rg][rh] : 0.f;
         T* orow = gout + ev_off(ev, q0 + q, h, DH);
 #pragma unroll
@@ -863,7 +863,7 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
   const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
   const int threads = (per_group + S::NE) * 32;
   dim3 grid;
-  if (p.packed) {
+  if (is_varlen(p)) {
     tile_prefix(p, S::BM, tile_start, st);
     const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
     grid = dim3((unsigned)upper, 1, groups);

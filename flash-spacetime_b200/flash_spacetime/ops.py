@@ -130,8 +130,12 @@ class _Problem:
         scale: Optional[float],
         use_attn_bias: bool,
         use_act_bias: bool,
+        layout: str = "bhld",
     ) -> None:
         self.packed = cu_seqlens is not None
+        if layout not in ("bhld", "blhd"):
+            raise ValueError(f"layout must be 'bhld' or 'blhd', got {layout!r}")
+        self.layout = "packed" if self.packed else layout
         if q.dtype not in _DTYPES:
             raise ValueError(f"unsupported dtype {q.dtype}")
         if not q.is_cuda:
@@ -149,8 +153,12 @@ class _Problem:
                 raise ValueError(f"varlen feats must be [T, F], got {tuple(feats.shape)}")
         else:
             if q.dim() != 4:
-                raise ValueError(f"q must be [B, H, L, D], got {tuple(q.shape)}")
-            batch, heads, length, dim = q.shape
+                raise ValueError(f"q must be [B, H, L, D] (or [B, L, H, D] with layout='blhd'), "
+                                 f"got {tuple(q.shape)}")
+            if self.layout == "blhd":
+                batch, length, heads, dim = q.shape
+            else:
+                batch, heads, length, dim = q.shape
             self.cu = None
             self.seq = seqlens.to(device=q.device, dtype=torch.int32).contiguous()
             if self.seq.shape != (batch,):
@@ -193,7 +201,7 @@ class _Problem:
     def c_struct(self) -> _lib.FstProblem:
         p = _lib.FstProblem()
         p.dtype = _DTYPES[self.dtype]
-        p.packed = int(self.packed)
+        p.packed = {"bhld": 0, "packed": 1, "blhd": 2}[self.layout]
         p.batch = self.batch
         p.heads = self.heads
         p.max_len = self.length
@@ -215,14 +223,9 @@ class _Problem:
     def stat_shape(self) -> Tuple[int, ...]:
         if self.packed:
             return (self.rows, self.heads)
+        if self.layout == "blhd":
+            return (self.batch, self.length, self.heads)
         return (self.batch, self.heads, self.length)
-
-    def valid_rows(self) -> Optional[Tensor]:
-        """``[B, 1, L, 1]`` bool of valid rows (padded layout), else None."""
-        if self.packed:
-            return None
-        pos = torch.arange(self.length, device=self.device)
-        return (pos[None, :] < self.seq[:, None])[:, None, :, None]
 
 
 def _workspace(nbytes: int, device: torch.device) -> Tuple[Optional[Tensor], int]:
@@ -324,6 +327,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         scale: Optional[float],
         use_attn_bias: bool,
         use_activation_bias: bool,
+        layout: str = "bhld",
     ) -> Tensor:
         if feats.requires_grad:
             raise ValueError("feats (detector data) must not require grad")
@@ -332,7 +336,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("q, k and v must have the same dtype")
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                      use_attn_bias, use_activation_bias)
+                      use_attn_bias, use_activation_bias, layout)
         qc, kc, vc = (_dense(t) for t in (q, k, v))
         out, lse = fused_forward(pb, qc, kc, vc)
         ctx.save_for_backward(qc, kc, vc, out, lse)
@@ -356,7 +360,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             g["dq"] if need[0] else None,
             g["dk"] if need[1] else None,
             g["dv"] if need[2] else None,
-            None, dw, db, None, None, None, None, None,
+            None, dw, db, None, None, None, None, None, None,
         )
 
 
@@ -373,6 +377,7 @@ def flash_spacetime_attention(
     use_activation_bias: bool = True,
     *,
     key_padding_mask: Optional[Tensor] = None,
+    layout: str = "bhld",
 ) -> Tensor:
     """Fused spacetime-bias attention on a padded batch (upstream forward.py:481-501).
 
@@ -382,18 +387,23 @@ def flash_spacetime_attention(
     (upstream's form); a ``[B, L]`` key-padding mask, bool (True = padding)
     or float (0 / -inf), is accepted there or as ``key_padding_mask=``.
     Returns ``[B, H, L, Dh]`` in q's dtype with padding rows exactly 0.
+
+    ``layout='blhd'`` (an addition) takes and returns ``[B, L, H, Dh]``: a
+    ``[B, L, H*Dh]`` projection viewed per head, with no head split or merge
+    around the op.
     """
+    length = q.shape[1] if layout == "blhd" else q.shape[2]
     if key_padding_mask is not None:
         if seqlens is not None:
             raise ValueError("pass seqlens or key_padding_mask, not both")
         seqlens = seqlens_from_mask(key_padding_mask)
     elif seqlens is None:
-        seqlens = torch.full((q.shape[0],), q.shape[2], dtype=torch.int32, device=q.device)
+        seqlens = torch.full((q.shape[0],), length, dtype=torch.int32, device=q.device)
     elif seqlens.dim() == 2:
         seqlens = seqlens_from_mask(seqlens)
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, seqlens, None,
-        scale, use_attn_bias, use_activation_bias,
+        scale, use_attn_bias, use_activation_bias, layout,
     )
 
 
@@ -465,10 +475,11 @@ def flash_spacetime_forward(
     use_attn_bias: bool = True,
     use_activation_bias: bool = True,
     cu_seqlens: Optional[Tensor] = None,
+    layout: str = "bhld",
 ) -> Tuple[Tensor, Tensor]:
     """Forward only, returning ``(out, lse)`` (upstream forward.py:222-346)."""
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                  use_attn_bias, use_activation_bias)
+                  use_attn_bias, use_activation_bias, layout)
     return fused_forward(pb, _dense(q), _dense(k), _dense(v))
 
 
@@ -488,6 +499,7 @@ def flash_spacetime_backward(
     use_activation_bias: bool = True,
     cu_seqlens: Optional[Tensor] = None,
     want_absmax: bool = False,
+    layout: str = "bhld",
 ) -> Dict[str, Optional[Tensor]]:
     """Backward only (upstream backward.py:488-630), with diagnostics.
 
@@ -495,6 +507,6 @@ def flash_spacetime_backward(
     by construction) and, with ``want_absmax``, ``ds_absmax`` (rowmax |dS|).
     """
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                  use_attn_bias, use_activation_bias)
+                  use_attn_bias, use_activation_bias, layout)
     return fused_backward(pb, _dense(q), _dense(k), _dense(v),
                           out, lse, grad_out, want_absmax)

@@ -34,6 +34,10 @@
  *   packed (packed == 1): q,k,v,u,out,dout,wt [T, H, D*] ; feats [T, fs]
  *                         lse/delta/sigma [T, H] ; event b is rows
  *                         [cu_seqlens[b], cu_seqlens[b+1]).
+ *   padded row-major (packed == 2): q,k,v,u,out,dout,wt [B, L, H, D*] ;
+ *                         feats [B, L, fs] ; lse/delta/sigma [B, L, H] ; the
+ *                         caller's [B, L, H*Dh] projections without a head
+ *                         split (no upstream counterpart); padding as for 0.
  * D* is Dh for q,k,v,out,dout and C for u, wt.
  */
 #ifndef FLASH_SPACETIME_H_
@@ -69,7 +73,7 @@ enum FstStatus {
  */
 typedef struct FstProblem {
   int32_t dtype;          /* enum FstDtype                                   */
-  int32_t packed;         /* 0 padded [B,H,L,*], 1 packed [T,H,*]            */
+  int32_t packed;         /* 0 padded [B,H,L,*], 1 packed [T,H,*], 2 [B,L,H,*] */
   int32_t batch;          /* B: number of events                             */
   int32_t heads;          /* H                                               */
   int32_t max_len;        /* padded: L. packed: an upper bound on any event  */

@@ -239,3 +239,29 @@ def test_nested_tensor_adapter_matches_varlen():
         res.append((out_v.detach().clone(), q.grad.clone(), k.grad.clone(), w.grad.clone()))
     for a, b in zip(res[0], res[1]):
         assert torch.equal(a, b)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_blhd_layout_matches_bhld(dtype):
+    # layout='blhd' reads [B, L, H, Dh] (a [B, L, H*Dh] projection per head)
+    # and must give the transposed BHLD results, gradients included, bitwise.
+    case = cs.padded_case(3, 70, 12, 32, 16, True, seed=321)
+    seq = case["seqlens"].cuda()
+    feats = case["feats"].cuda()
+    go = torch.randn(case["q"].shape, generator=torch.Generator().manual_seed(3)).to("cuda", dtype)
+    res = {}
+    for layout in ("bhld", "blhd"):
+        q, k, v = (_to(case[x], dtype) for x in ("q", "k", "v"))
+        g = go
+        if layout == "blhd":
+            q, k, v, g = (t.transpose(1, 2).contiguous() for t in (q, k, v, g))
+        q.requires_grad_(True)
+        k.requires_grad_(True)
+        w = _to(case["weight"], torch.float32).requires_grad_(True)
+        b = _to(case["bias"], torch.float32).requires_grad_(True)
+        out = flash_spacetime_attention(q, k, v, feats, w, b, seq, layout=layout)
+        out.backward(g)
+        tr = (lambda t: t.transpose(1, 2)) if layout == "blhd" else (lambda t: t)
+        res[layout] = (tr(out.detach()), tr(q.grad), tr(k.grad), w.grad.clone(), b.grad.clone())
+    for a, b_ in zip(res["bhld"], res["blhd"]):
+        assert torch.equal(a, b_)

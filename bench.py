@@ -412,7 +412,9 @@ def run_ours(args):
                    "head_dim": DIM, "channels": CHANNELS,
                    "padded_length": padlen, "coords": args.coords,
                    "valid_pairs_per_gpu": flops["pairs"],
-                   "l2_policy": "inputs larger than L2 (q, k, v, grad 151 MB each)"},
+                   "l2_policy": f"inputs larger than L2 (q, k, v, grad "
+                                f"{data['q'].numel() * data['q'].element_size() / 1e6:.0f} MB "
+                                f"each)"},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "peak_gib": peak_gib,
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",

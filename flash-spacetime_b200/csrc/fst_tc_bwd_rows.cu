@@ -63,7 +63,10 @@ struct RowShape {
   // bias tile: per (q, h) 16 keys x (u.E, w~.E) fp32 + 16 pad words.
   static constexpr int BROW = 48;
   static constexpr int BQ = HP * BROW + 16;
-  static constexpr int PQ = 16 * 8 + 4;  // P tile words per query (16 heads x 16 keys)
+  // P tiles: per query 16 head rows of 16 keys (8 words) padded to 12 words,
+  // + 4 pad words per query (conflict-free ldmatrix rows and stores).
+  static constexpr int PH = 12;
+  static constexpr int PQ = 16 * PH + 4;
 
   // The union region holds, in turn: staged Q and dO (phase 1), staged u and
   // w~ (phase 2), the loop's bias and P tiles, and the epilogue's H and G.
@@ -601,7 +604,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         uint32_t pp[4], pd[4];
         const int mi = lane >> 3;
         const int h = (mi & 1) * 8 + (lane & 7);
-        const uint32_t po = (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4;
+        const uint32_t po = (q * S::PQ + h * S::PH + (mi >> 1) * 4) * 4;
         ldsm_x4(sm + S::OFF_P + (2 * s) * S::SZ_P + po, pp);
         ldsm_x4(sm + S::OFF_P + (2 * s + 1) * S::SZ_P + po, pd);
 #pragma unroll
@@ -842,8 +845,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
       if (n >= 2) named_sync(rb_p_empty(s), NBAR);
       {
-        const uint32_t pb = sm + S::OFF_P + (2 * s) * S::SZ_P + (hl * 8 + m4) * 4;
-        const uint32_t db = sm + S::OFF_P + (2 * s + 1) * S::SZ_P + (hl * 8 + m4) * 4;
+        const uint32_t pb = sm + S::OFF_P + (2 * s) * S::SZ_P + (hl * S::PH + m4) * 4;
+        const uint32_t db = sm + S::OFF_P + (2 * s + 1) * S::SZ_P + (hl * S::PH + m4) * 4;
         sts_u32(pb + r8 * S::PQ * 4, pp[0]);
         sts_u32(pb + r8 * S::PQ * 4 + 16, pp[2]);
         sts_u32(pb + (r8 + 8) * S::PQ * 4, pp[1]);

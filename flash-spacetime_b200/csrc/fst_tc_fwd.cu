@@ -77,8 +77,12 @@ struct FwdShape {
   // free of bank conflicts.
   static constexpr int BROW = 24;
   static constexpr int BQ = ((HP * BROW + 31) / 32) * 32 + 8;
-  // P tile: per query 16 head rows x 8 words (16 keys) + 4 pad words.
-  static constexpr int PQ = 16 * 8 + 4;
+  // P tile: per query 16 head rows of 16 keys (8 words) padded to 12 words,
+  // + 4 pad words per query: the E warps' ldmatrix rows (one per head) then
+  // fall in distinct bank groups, and the head warps' stores stay
+  // conflict-free.
+  static constexpr int PH = 12;
+  static constexpr int PQ = 16 * PH + 4;
 
   // Shared memory carve-up (bytes). The Q and u staging tiles are read into
   // registers once, before the key loop; the bias / P / alpha exchange tiles
@@ -453,7 +457,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         {
           const int mi = lane >> 3;
           const int h = (mi & 1) * 8 + (lane & 7);
-          ldsm_x4(sP + s * S::SZ_P + (q * S::PQ + h * 8 + (mi >> 1) * 4) * 4, pa);
+          ldsm_x4(sP + s * S::SZ_P + (q * S::PQ + h * S::PH + (mi >> 1) * 4) * 4, pa);
         }
 #pragma unroll
         for (int nc = 0; nc < S::NTC; ++nc) {
@@ -711,7 +715,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 
       if (act) {
         if (n >= 2) named_sync(bar_p_empty(s), NBAR);
-        const uint32_t pbase = sP + s * S::SZ_P + (hl * 8 + m4) * 4;
+        const uint32_t pbase = sP + s * S::SZ_P + (hl * S::PH + m4) * 4;
 #pragma unroll
         for (int rg = 0; rg < S::RG; ++rg) {
           const int q = rg * 16 + r8;

@@ -54,6 +54,11 @@ int check_problem(const FstProblem* p) {
   if (p->packed == 1) {
     if (!p->cu_seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "packed needs cu_seqlens");
   } else {
+    // Padded grids put the events on grid.y (tiles of one event run next to
+    // each other, which balances the SMs best); grid.y stops at 65535.
+    if (p->batch > 65535)
+      return fail(FST_ERR_UNSUPPORTED,
+                  "padded batch of %d events: at most 65535 (use the packed layout)", p->batch);
     if (!p->seqlens && p->batch > 0) return fail(FST_ERR_INVALID, "padded needs seqlens");
     if ((int64_t)p->batch * p->max_len != p->total_rows)
       return fail(FST_ERR_INVALID, "padded total_rows must equal B*L");

@@ -98,3 +98,17 @@ def test_misaligned_tensor_core_inputs_are_rejected(which):
     assert rc == _lib.FST_ERR_INVALID
     msg = _lib.last_error()
     assert ("16-byte" in msg) or ("multiple of 4" in msg), msg
+
+
+def test_padded_batch_limit_is_reported():
+    # More than 65535 events in a padded layout is refused before any launch
+    # (the packed layout has no such limit).
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.packed, p.batch, p.heads, p.max_len = 1, 0, 70000, 1, 1
+    p.head_dim, p.channels, p.feat_stride, p.total_rows = 32, 16, 4, 70000
+    a = _lib.FstForwardArgs()
+    a.prob = p
+    rc = lib.fst_forward(ctypes.byref(a), None)
+    assert rc == _lib.FST_ERR_UNSUPPORTED
+    assert "65535" in _lib.last_error()

@@ -96,7 +96,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 
   int b, kb;
   if (!is_varlen(p)) {
-    b = blockIdx.y;
+    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
     kb = blockIdx.x;
   } else {
     const int t = blockIdx.x;

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
 
   int b, qb;
   if (!is_varlen(p)) {
-    b = blockIdx.y;
+    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
     qb = blockIdx.x;
   } else {
     const int t = blockIdx.x;

@@ -130,7 +130,7 @@ __device__ __forceinline__ int bar_p_empty(int s) { return 7 + s; }
 __device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_start, int& b,
                                          int& qb) {
   if (!is_varlen(p)) {
-    b = blockIdx.y;
+    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
     qb = blockIdx.x;
     return true;
   }

@@ -21,7 +21,7 @@ FST_ERR_CUDA = 3
 FST_ERR_WORKSPACE = 4
 FST_ERR_DEVICE = 5
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 
 EXPORTED = (
     "fst_abi_version",
@@ -56,6 +56,7 @@ class FstProblem(ctypes.Structure):
         ("freqs", ctypes.c_void_p),
         ("weight", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
+        ("event_order", ctypes.c_void_p),
     ]
 
 

@@ -148,6 +148,7 @@ class _Problem:
             batch = self.cu.numel() - 1
             length = 0
             self.seq = None
+            self.order = None
             rows = total
             if feats.dim() != 2 or feats.shape[0] != total:
                 raise ValueError(f"varlen feats must be [T, F], got {tuple(feats.shape)}")
@@ -164,6 +165,10 @@ class _Problem:
             if self.seq.shape != (batch,):
                 raise ValueError(f"seqlens must be [B] = [{batch}], got {tuple(self.seq.shape)}")
             rows = batch * length
+            # Longest events first: their row / key blocks are scheduled
+            # before the short ones', which balances the SMs (the results
+            # do not depend on the order; the sort is stable).
+            self.order = torch.argsort(self.seq, descending=True, stable=True).to(torch.int32)
             if feats.dim() != 3 or feats.shape[:2] != (batch, length):
                 raise ValueError(f"feats must be [B, L, F], got {tuple(feats.shape)}")
         if feats.shape[-1] < 4:
@@ -218,6 +223,7 @@ class _Problem:
         p.freqs = _ptr(self.freqs)
         p.weight = _ptr(self.w32)
         p.bias = _ptr(self.b32)
+        p.event_order = _ptr(self.order)
         return p
 
     def stat_shape(self) -> Tuple[int, ...]:

@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FST_ABI_VERSION 2
+#define FST_ABI_VERSION 3
 
 /* Storage dtype of q, k, v, u, wt, out, dout, dq, dk, dv. */
 enum FstDtype { FST_F32 = 0, FST_BF16 = 1, FST_F16 = 2 };
@@ -91,6 +91,11 @@ typedef struct FstProblem {
   const float* freqs;        /* [C/2] device fp32 frequency ladder            */
   const float* weight;       /* [Dh, C] device fp32 (nn.Linear layout)        */
   const float* bias;         /* [Dh] device fp32, or NULL                     */
+  /* Padded layouts: optional [B] device permutation of the events, the order
+   * in which the kernels' row / key blocks are scheduled (longest first
+   * balances the SMs); NULL = natural order. Results do not depend on it.
+   * No upstream counterpart. */
+  const int32_t* event_order;
 } FstProblem;
 
 typedef struct FstForwardArgs {

@@ -26,8 +26,9 @@ namespace tc {
 bool fwd_supported(const FstProblem& p);
 size_t fwd_workspace(const FstProblem& p);
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
-// Exclusive prefix of ceil(len_b / bm) over the events of a packed batch,
-// written to tile_start[0..B] (one small kernel; no host synchronisation).
+// Exclusive prefix of ceil(len_b / bm) over the events of a packed batch, in
+// p.event_order when given, written to tile_start[0..B] (one small kernel; no
+// host synchronisation).
 void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st);
 int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, void* u_ws,
                     void* wt_ws, void* qt_ws);

@@ -106,8 +106,8 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       int mid = (lo + hi + 1) >> 1;
       if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    b = lo;
-    kb = t - tile_start[b];
+    kb = t - tile_start[lo];
+    b = p.event_order ? p.event_order[lo] : lo;
   }
   const EventSpan ev = event_span(p, b);
   const int k0 = kb * S::BK;

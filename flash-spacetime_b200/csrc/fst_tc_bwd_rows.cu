@@ -144,8 +144,8 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       int mid = (lo + hi + 1) >> 1;
       if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
     }
-    b = lo;
-    qb = t - tile_start[b];
+    qb = t - tile_start[lo];
+    b = p.event_order ? p.event_order[lo] : lo;
   }
   const int64_t part = is_varlen(p) ? ((int64_t)blockIdx.z * gridDim.x + blockIdx.x)
                                 : (((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x +

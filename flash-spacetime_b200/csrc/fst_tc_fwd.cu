@@ -141,8 +141,8 @@ __device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_st
     int mid = (lo + hi + 1) >> 1;
     if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
   }
-  b = lo;
-  qb = t - tile_start[b];
+  qb = t - tile_start[lo];
+  b = p.event_order ? p.event_order[lo] : lo;
   return true;
 }
 
@@ -812,16 +812,19 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 
 // ---------------------------------------------------------------------------
 
-__global__ void tile_prefix_kernel(const int32_t* __restrict__ cu, int batch, int bm,
+__global__ void tile_prefix_kernel(const int32_t* __restrict__ cu,
+                                   const int32_t* __restrict__ order, int batch, int bm,
                                    int* __restrict__ tile_start) {
-  // Single-CTA exclusive scan of ceil(len_b / bm) over the events.
+  // Single-CTA exclusive scan of ceil(len_b / bm) over the events, taken in
+  // the given order (position k holds event order[k]) or the natural one.
   __shared__ int warp_sums[32];
   __shared__ int carry;
   if (threadIdx.x == 0) carry = 0;
   __syncthreads();
   for (int base = 0; base < batch; base += blockDim.x) {
     const int b = base + threadIdx.x;
-    const int v = b < batch ? (cu[b + 1] - cu[b] + bm - 1) / bm : 0;
+    const int ev = b < batch ? (order ? order[b] : b) : 0;
+    const int v = b < batch ? (cu[ev + 1] - cu[ev] + bm - 1) / bm : 0;
     int x = v;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
@@ -851,7 +854,7 @@ __global__ void tile_prefix_kernel(const int32_t* __restrict__ cu, int batch, in
 }
 
 void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st) {
-  tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.batch, bm, tile_start);
+  tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.event_order, p.batch, bm, tile_start);
   count_launch();
 }
 

@@ -148,7 +148,9 @@ class _Problem:
             batch = self.cu.numel() - 1
             length = 0
             self.seq = None
-            self.order = None
+            # Longest events first (see the padded case below).
+            lens = self.cu[1:] - self.cu[:-1]
+            self.order = torch.argsort(lens, descending=True, stable=True).to(torch.int32)
             rows = total
             if feats.dim() != 2 or feats.shape[0] != total:
                 raise ValueError(f"varlen feats must be [T, F], got {tuple(feats.shape)}")

@@ -91,10 +91,10 @@ typedef struct FstProblem {
   const float* freqs;        /* [C/2] device fp32 frequency ladder            */
   const float* weight;       /* [Dh, C] device fp32 (nn.Linear layout)        */
   const float* bias;         /* [Dh] device fp32, or NULL                     */
-  /* Padded layouts: optional [B] device permutation of the events, the order
-   * in which the kernels' row / key blocks are scheduled (longest first
-   * balances the SMs); NULL = natural order. Results do not depend on it.
-   * No upstream counterpart. */
+  /* Optional [B] device permutation of the events: the order in which the
+   * kernels' row / key blocks are scheduled (longest first balances the SMs);
+   * NULL = natural order. Results do not depend on it. No upstream
+   * counterpart. */
   const int32_t* event_order;
 } FstProblem;
 

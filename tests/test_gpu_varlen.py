@@ -265,3 +265,27 @@ def test_blhd_layout_matches_bhld(dtype):
         res[layout] = (tr(out.detach()), tr(q.grad), tr(k.grad), w.grad.clone(), b.grad.clone())
     for a, b_ in zip(res["bhld"], res["blhd"]):
         assert torch.equal(a, b_)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_empty_and_equal_length_events(dtype):
+    # Zero-length events (no rows at all) and ties in length (the scheduling
+    # order is a stable longest-first sort): packed and padded agree bitwise,
+    # padding rows are 0, and the valid rows follow the float64 oracle.
+    lengths = [40, 0, 17, 40, 0, 1, 17]
+    case = cs.packed_case(lengths, 12, 32, 16, seed=55)
+    seqlens = torch.tensor(lengths, device="cuda")
+    w, b = _to(case["weight"], torch.float32), _to(case["bias"], torch.float32)
+    out_v = flash_spacetime_attention_varlen(
+        _to(case["q"], dtype), _to(case["k"], dtype), _to(case["v"], dtype),
+        case["feats"].cuda(), w, b, case["cu"].cuda())
+    out_p = flash_spacetime_attention(
+        _to(_pad(case, "q"), dtype), _to(_pad(case, "k"), dtype), _to(_pad(case, "v"), dtype),
+        _pad(case, "feats").cuda(), w, b, seqlens)
+    assert torch.equal(out_v, _unpad(out_p, lengths))
+    for i, n in enumerate(lengths):
+        assert torch.count_nonzero(out_p[i, :, n:]) == 0
+    ref = orc.oracle_packed(case["q"], case["k"], case["v"], case["feats"], case["weight"],
+                            case["bias"], case["cu"].tolist())
+    err = cs.normwise(out_v.double().cpu(), ref["out"])
+    assert err <= cs.NORMWISE[dtype] if dtype != torch.float32 else err <= 1e-3

@@ -1,7 +1,6 @@
 // Device building blocks of the tensor-core kernels (sm_100a):
-// warp-level bf16/fp16 MMA, ldmatrix/movmatrix, cp.async with mbarrier
-// completion, named barriers, bounded mbarrier waits and the sin/cos of the
-// pair embedding.
+// warp-level bf16/fp16 MMA, ldmatrix/movmatrix, cp.async, named barriers,
+// the sin/cos of the pair embedding and the tensor-core projection.
 #pragma once
 
 #include <cuda_bf16.h>
@@ -136,46 +135,6 @@ template <int N>
 __device__ __forceinline__ void cp_async_wait() {
   asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
-// Arrive on `bar` once all of this thread's prior cp.async copies completed.
-__device__ __forceinline__ void cp_async_arrive(uint32_t bar) {
-  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t bar, int count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t bar) {
-  asm volatile("{ .reg .b64 st; mbarrier.arrive.shared::cta.b64 st, [%0]; }\n" ::"r"(bar)
-               : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{ .reg .pred p; mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2; selp.u32 %0, 1, 0, p; }\n"
-      : "=r"(ok)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Error bits a kernel ORs into the caller's status word.
-constexpr int kErrTimeout = 1;
-
-// Spin on an mbarrier phase with an iteration cap (each try_wait already
-// suspends for a hardware-chosen interval). On timeout the status word gets
-// kErrTimeout and the caller carries on with whatever is in shared memory:
-// the kernel always terminates and the host reports the error.
-constexpr long kSpinLimit = 1L << 26;
-__device__ __forceinline__ void mbar_wait(uint32_t bar, uint32_t parity, int* status) {
-  long it = 0;
-  while (!mbar_try_wait(bar, parity)) {
-    if (++it > kSpinLimit) {
-      if (status) atomicOr(status, kErrTimeout);
-      return;
-    }
-  }
-}
-
 __device__ __forceinline__ void named_sync(int id, int nthreads) {
   asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
 }

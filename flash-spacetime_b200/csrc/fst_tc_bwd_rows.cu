@@ -549,8 +549,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
           const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
-#pragma unroll
-            for (int r = 0; r < 2; ++r) sincos_xf(xt, fr[g][r], fv[g][r], sn[nt][g][r], cs[nt][g][r]);
+            sincos_xf2(xt, fr[g], fv[g], sn[nt][g], cs[nt][g]);
         }
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt)

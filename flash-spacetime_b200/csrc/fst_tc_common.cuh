@@ -167,6 +167,38 @@ __device__ __forceinline__ void sincos_xf(float x, float f, float f_rev, float& 
   c = __cosf(r);
 }
 
+// sincos_xf for two frequencies at once: the same operations, issued as the
+// packed two-lane fp32 instructions of sm_100 (fma/sub/mul .rn.f32x2), so the
+// reduction of both arguments costs the issue slots of one.
+__device__ __forceinline__ uint64_t f2pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2unpack(uint64_t v, float& lo, float& hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ void sincos_xf2(float x, const float (&f)[2], const float (&f_rev)[2],
+                                           float (&s)[2], float (&c)[2]) {
+  const uint64_t x2 = f2pack(x, x);
+  const uint64_t fr2 = f2pack(f_rev[0], f_rev[1]), f2 = f2pack(f[0], f[1]);
+  const uint64_t kRound2 = f2pack(12582912.f, 12582912.f);  // 1.5 * 2^23
+  const uint64_t kNegC1 = f2pack(-6.28125f, -6.28125f);
+  const uint64_t kNegC2 = f2pack(-1.9353071795864769e-03f, -1.9353071795864769e-03f);
+  uint64_t n2, m2, r2;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(n2) : "l"(x2), "l"(fr2), "l"(kRound2));
+  asm("sub.rn.f32x2 %0, %0, %1;" : "+l"(n2) : "l"(kRound2));
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(m2) : "l"(n2), "l"(kNegC1));
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r2) : "l"(x2), "l"(f2), "l"(m2));
+  asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(r2) : "l"(n2), "l"(kNegC2));
+  float r0, r1;
+  f2unpack(r2, r0, r1);
+  s[0] = __sinf(r0);
+  c[0] = __cosf(r0);
+  s[1] = __sinf(r1);
+  c[1] = __cosf(r1);
+}
+
 // x_ij for the 16-bit kernels: as pair_angle, with the square root taken by
 // sqrt.approx (one MUFU op) and the clip applied before it -- |I| >= 16 maps
 // straight to +-4096, the exact value the clipped branch takes.

@@ -28,6 +28,9 @@
 // cores), E warps own QPE rows for all heads (embedding, the two logit-side
 // bias products u.E and w~.E, and H', G), and the per-chunk bias tiles and P
 // tiles cross between the two groups through double-buffered shared memory.
+// The prologue forms u = (q*scale) W and w~ = dO W on the tensor cores and
+// writes them, with qt = [q*scale], to the workspace for the column kernel;
+// the epilogue forms this CTA's dW / db partials on the tensor cores.
 
 #include <cuda_runtime.h>
 

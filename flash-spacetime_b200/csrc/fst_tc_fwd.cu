@@ -4,16 +4,18 @@
 // What it computes is upstream's flash_spacetime_fwd_kernel
 // (src/flash_spacetime/forward.py:63-219) plus the host epilogue of
 // flash_spacetime_forward (forward.py:333-345):
-//   s_ij = qt_i . k_j + u_i . E_ij           (u = (q*scale) W, from the host)
+//   s_ij = qt_i . k_j + u_i . E_ij           (u = (q*scale) W, formed in the prologue)
 //   P    = online softmax over the event's keys
 //   out  = sum_j P v_j / l + (sum_j P E_ij / l) W^T + b,  lse = log sum_j exp s
 //
 // How it is laid out on B200 (one CTA = one event x BM queries x <= 12 heads):
 //
-//   head warps  (one per head): own BM query rows of their head. They run
-//               QK^T and PV on the tensor cores (m16n8k16, fp32 accumulate,
-//               O in registers), add the pair bias, and do the online
-//               softmax with exp2 on the MUFU pipe.
+//   head warps  (one per head): own BM query rows of their head. They form
+//               u = (q*scale) W for their head in the prologue, run QK^T and
+//               PV on the tensor cores (m16n8k16, fp32 accumulate, O in
+//               registers), add the pair bias, and do the online softmax with
+//               exp2 on the MUFU pipe (the reference max of a row moves only
+//               when it grows by more than 2^8).
 //   E warps     (BM / QPE of them): own QPE query rows each, all heads. They
 //               evaluate the C-channel embedding E_ij of every pair once (not
 //               once per head) directly in mma B-fragment order, form the
@@ -30,8 +32,10 @@
 // The two consumer groups exchange, per chunk, the fp32 bias tile (E warps
 // -> head warps) and the bf16/fp16 P tile plus the online-softmax rescale
 // factors (head warps -> E warps) through double-buffered shared memory,
-// handed over with named barriers (full/empty pairs). The embedding is never
-// written to memory and nothing of size O(L^2) exists anywhere.
+// handed over with named barriers (full/empty pairs). At Dh <= 32, C <= 16
+// the E warps run one chunk ahead (the bias of chunk n+1 is ready before the
+// head warps finish chunk n). The embedding is never written to memory and
+// nothing of size O(L^2) exists anywhere.
 //
 // There are no spin waits: cp.async completion is awaited per thread and
 // every named barrier is reached by all head and E warps in the same order.

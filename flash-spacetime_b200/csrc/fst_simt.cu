@@ -63,14 +63,16 @@ __device__ __forceinline__ void embed(float x, const float* freqs, int C, float*
   }
 }
 
-// sum_d x[d] W[d][c] in fp32, rounded to T as the host-side projection is.
+// sum_d (x[off + d] * mul) W[d][c] in fp32, rounded to T as the host-side
+// projection is. x is read from global memory with a rolled loop: inlined
+// into the unrolled channel loops of the callers, a fully unrolled d loop
+// would make the compiler process Dh x C (64 x 64) bodies per call site.
 template <typename T>
-__device__ __forceinline__ float project(const FstProblem& p, const float* x, int c, int D, int C,
-                                         T) {
+__device__ __forceinline__ float project(const FstProblem& p, const T* __restrict__ x, int64_t off,
+                                         float mul, int c, int D, int C) {
   float acc = 0.f;
-#pragma unroll
-  for (int d = 0; d < kMax; ++d)
-    if (d < D) acc = fmaf(x[d], p.weight[(int64_t)d * C + c], acc);
+#pragma unroll 1
+  for (int d = 0; d < D; ++d) acc = fmaf(to_f<T>(x[off + d]) * mul, p.weight[(int64_t)d * C + c], acc);
   return to_f<T>(from_f<T>(acc));
 }
 
@@ -102,7 +104,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
 #pragma unroll
   for (int c = 0; c < kMax; ++c) {
     uu[c] = (p.use_attn_bias && c < C)
-                ? (u ? to_f<T>(u[uoff + c]) : project(p, qt, c, D, C, from_f<T>(0.f)))
+                ? (u ? to_f<T>(u[uoff + c]) : project<T>(p, q, off, p.scale, c, D, C))
                 : 0.f;
     ae[c] = 0.f;
     e[c] = 0.f;
@@ -191,9 +193,9 @@ __device__ __forceinline__ void load_bwd_row(const FstBackwardArgs& a, int64_t r
     r.uu[c] = 0.f;
     r.wt[c] = 0.f;
     if (c < C && p.use_attn_bias)
-      r.uu[c] = a.u ? to_f<T>(((const T*)a.u)[coff + c]) : project(p, r.qt, c, D, C, T());
+      r.uu[c] = a.u ? to_f<T>(((const T*)a.u)[coff + c]) : project<T>(p, q, off, p.scale, c, D, C);
     if (c < C && p.use_act_bias)
-      r.wt[c] = a.wt ? to_f<T>(((const T*)a.wt)[coff + c]) : project(p, r.dov, c, D, C, T());
+      r.wt[c] = a.wt ? to_f<T>(((const T*)a.wt)[coff + c]) : project<T>(p, dout, off, 1.f, c, D, C);
   }
   r.off = c;
   r.lse = a.lse[stat_off(p, row, h)];

@@ -223,24 +223,37 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, data, index, step, device, world, total_flops):
+def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, expect):
     """The step through the public API with every input copied from pinned
     host memory inside the timed region and dW/db read back each step.
 
     As a training loop's data loader would, the copy of step i+1's inputs is
     issued on a side stream while step i computes (two device slots, ordered
     by events); every step's own host->device copy is inside the timed region.
+    A padded batch ships only its valid rows (``upload_valid_rows``, a gather
+    kernel reading the pinned host rows; the kernels never read a padding
+    row). The
+    last step's dW/db must equal ``expect`` (the device-resident run's) bit
+    for bit.
     """
+    from flash_spacetime import ops
     from flash_spacetime.sharding import max_over_ranks
 
     keys = ("q", "k", "v", "grad", "feats", "weight", "bias")
     host = {k: data[k].detach().cpu().pin_memory() for k in keys}
     host["index"] = index.cpu().pin_memory()
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    rows = ("q", "k", "v", "grad", "feats") if padded else ()
+    h2d = 0
+    for k, t in host.items():
+        if k in rows:  # [B, H, L, D] or [B, L, 4]: sum(lens) rows of numel / (B L) elements
+            length = t.shape[2] if t.dim() == 4 else t.shape[1]
+            h2d += sum(lens) * (t.numel() // (t.shape[0] * length)) * t.element_size()
+        else:
+            h2d += t.numel() * t.element_size()
     dw_host = torch.empty(DIM * CHANNELS + DIM, dtype=torch.float32).pin_memory()
     d2h = dw_host.numel() * dw_host.element_size()
 
-    slots = [{k: torch.empty_like(t, device=device) for k, t in host.items()} for _ in range(2)]
+    slots = [{k: torch.zeros_like(t, device=device) for k, t in host.items()} for _ in range(2)]
     copy_stream = torch.cuda.Stream(device)
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
@@ -251,7 +264,10 @@ def run_e2e(args, data, index, step, device, world, total_flops):
         with torch.cuda.stream(copy_stream):
             copy_stream.wait_event(free[slot])  # the step that used this slot is done
             for k, t in host.items():
-                slots[slot][k].copy_(t, non_blocking=True)
+                if k in rows:
+                    ops.upload_valid_rows(slots[slot][k], t, lens)
+                else:
+                    slots[slot][k].copy_(t, non_blocking=True)
             ready[slot].record(copy_stream)
 
     def run(n):
@@ -281,9 +297,13 @@ def run_e2e(args, data, index, step, device, world, total_flops):
     e1.record()
     torch.cuda.synchronize()
     e2e_ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, device)
+    if not torch.equal(dw_host, expect.cpu()):
+        raise RuntimeError("e2e: dW/db differ from the device-resident run")
     return {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-            "overlap": "next step's host->device copy on a side stream"}
+            "overlap": "next step's host->device copy on a side stream",
+            "transfer": ("valid rows only (upload_valid_rows: gather kernel reading pinned "
+                         "host memory)" if padded else "whole tensors")}
 
 
 def run_ours(args):
@@ -352,7 +372,7 @@ def run_ours(args):
     ev1 = torch.cuda.Event(enable_timing=True)
     ev0.record()
     for _ in range(args.steps):
-        step(leaves, feats, grad, index)
+        _, dw_last, db_last = step(leaves, feats, grad, index)
     ev1.record()
     torch.cuda.synchronize()
     if world > 1:
@@ -377,7 +397,9 @@ def run_ours(args):
     # End to end: inputs from pinned host memory every step, dW read back.
     e2e = None
     if not args.no_e2e:
-        e2e = run_e2e(args, data, index, step, device, world, total_flops)
+        expect = torch.cat([dw_last.flatten().float(), db_last.flatten().float()])
+        e2e = run_e2e(args, data, index, step, device, world, total_flops, lens,
+                      padlen is not None, expect)
 
     if world > 1:
         dist.barrier()

@@ -55,7 +55,7 @@ def __getattr__(name: str) -> object:
     """Resolve the fused entry points lazily (they need the CUDA library)."""
     if name in ("flash_spacetime_attention", "flash_spacetime_attention_varlen",
                 "flash_spacetime_attention_nested", "flash_spacetime_forward",
-                "flash_spacetime_backward"):
+                "flash_spacetime_backward", "upload_valid_rows"):
         from . import ops
 
         return getattr(ops, name)

@@ -31,6 +31,7 @@ EXPORTED = (
     "fst_forward",
     "fst_backward",
     "fst_forward_noalloc",
+    "fst_upload_rows",
     "fst_kernel_launches",
     "fst_last_error",
 )
@@ -129,6 +130,10 @@ def load() -> ctypes.CDLL:
         lib.fst_backward.argtypes = [ctypes.POINTER(FstBackwardArgs), ctypes.c_void_p]
         lib.fst_forward_noalloc.restype = ctypes.c_int
         lib.fst_forward_noalloc.argtypes = [ctypes.POINTER(FstForwardArgs), ctypes.c_void_p]
+        lib.fst_upload_rows.restype = ctypes.c_int
+        lib.fst_upload_rows.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                        ctypes.c_int64, ctypes.c_int64, ctypes.c_int64,
+                                        ctypes.c_int64, ctypes.c_void_p]
         lib.fst_kernel_launches.restype = ctypes.c_int64
         lib.fst_last_error.restype = ctypes.c_int
         lib.fst_last_error.argtypes = [ctypes.c_char_p, ctypes.c_size_t]

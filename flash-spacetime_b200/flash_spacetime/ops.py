@@ -22,7 +22,8 @@ Conventions kept from upstream:
 """
 
 import ctypes
-from typing import Any, Dict, Optional, Tuple
+import math
+from typing import Any, Dict, Optional, Sequence, Tuple
 
 import torch
 from torch import Tensor
@@ -518,3 +519,45 @@ def flash_spacetime_backward(
                   use_attn_bias, use_activation_bias, layout)
     return fused_backward(pb, _dense(q), _dense(k), _dense(v),
                           out, lse, grad_out, want_absmax)
+
+
+def upload_valid_rows(dst: Tensor, src: Tensor, seqlens: Sequence[int], layout: str = "bhld") -> Tensor:
+    """Copy the valid rows of a padded host batch ``src`` into the device tensor ``dst``.
+
+    A data-loader helper (upstream leaves the transfer to ``tensor.to(device)``):
+    with short events in a long padded batch most rows are padding, and the
+    fused kernels never read a padding row of q, k, v, feats or grad_out, so
+    only rows ``i < seqlens[b]`` of each event cross the host link. The
+    padding rows of ``dst`` keep whatever they held. A pinned ``src`` is read
+    by a gather kernel straight from host memory (asynchronous); a pageable
+    one by one 2D copy per event. ``src`` is a contiguous
+    CPU tensor, ``dst`` a contiguous CUDA
+    tensor of the same shape and dtype; ``seqlens`` are host integers. Shapes:
+    ``[B, H, L, D]`` with ``layout="bhld"``, or ``[B, L, ...]`` (feats, or the
+    ``"blhd"`` layout). The copy is ordered on the current stream. Returns
+    ``dst``.
+    """
+    if src.device.type != "cpu" or dst.device.type != "cuda":
+        raise ValueError("upload_valid_rows: src must be a CPU tensor and dst a CUDA tensor")
+    if src.shape != dst.shape or src.dtype != dst.dtype:
+        raise ValueError(f"upload_valid_rows: src {tuple(src.shape)} {src.dtype} does not "
+                         f"match dst {tuple(dst.shape)} {dst.dtype}")
+    if not (src.is_contiguous() and dst.is_contiguous()):
+        raise ValueError("upload_valid_rows: src and dst must be contiguous")
+    if layout not in ("bhld", "blhd"):
+        raise ValueError(f"upload_valid_rows: layout {layout!r} is not 'bhld' or 'blhd'")
+    lens = torch.as_tensor(seqlens, dtype=torch.int32, device="cpu").contiguous()
+    if lens.dim() != 1 or src.dim() < 3 or lens.numel() != src.shape[0]:
+        raise ValueError("upload_valid_rows: expected [B, ...] tensors and B host lengths")
+    es = src.element_size()
+    if layout == "bhld" and src.dim() == 4:
+        groups, max_len, row = src.shape[1], src.shape[2], src.shape[3] * es
+    else:
+        groups, max_len = 1, src.shape[1]
+        row = es * math.prod(src.shape[2:])
+    lib = _lib.load()
+    with torch.cuda.device(dst.device):
+        rc = lib.fst_upload_rows(_ptr(dst), _ptr(src), lens.data_ptr(), lens.numel(), groups,
+                                 max_len, row, _stream(dst.device))
+    _lib.check(rc, "fst_upload_rows")
+    return dst

@@ -165,6 +165,19 @@ int fst_backward(const FstBackwardArgs* args, void* stream);
  * array: calls that overlap on the GPU race, so order them on one stream. */
 int fst_forward_noalloc(const FstForwardArgs* args, void* stream);
 
+/* Host -> device copy of the valid rows of a padded batch (a data-loader
+ * helper; upstream leaves the transfer to the caller's tensor.to(device)).
+ * src (host, pinned for an asynchronous copy) and dst (device) are both
+ * [batch][groups][max_len][row_bytes]; for event b only rows < lens[b] of each
+ * group are copied, one 2D copy per event on `stream`. The padding rows of dst
+ * are left as they are: fst_forward / fst_backward never read the padding
+ * rows of q, k, v, feats or dout. lens is a HOST array of batch lengths, each
+ * in [0, max_len] (checked before any copy is issued). For [B, H, L, D]
+ * tensors groups = H and row_bytes = D * element size; for feats [B, L, fs]
+ * groups = 1 and row_bytes = fs * 4. */
+int fst_upload_rows(void* dst, const void* src, const int32_t* lens, int64_t batch,
+                    int64_t groups, int64_t max_len, int64_t row_bytes, void* stream);
+
 /* Number of CUDA kernels this library has launched in the process so far
  * (benchmark bookkeeping; no counterpart upstream). */
 int64_t fst_kernel_launches(void);

@@ -112,3 +112,28 @@ def test_padded_batch_limit_is_reported():
     rc = lib.fst_forward(ctypes.byref(a), None)
     assert rc == _lib.FST_ERR_UNSUPPORTED
     assert "65535" in _lib.last_error()
+
+
+def test_upload_rows_rejects_bad_lengths_before_copying():
+    # Every length is checked before the first copy is issued, so these calls
+    # make no CUDA call at all (the pointers are never dereferenced).
+    import torch
+    lib = _lib.load()
+    lens = torch.tensor([3, 9], dtype=torch.int32)
+    rc = lib.fst_upload_rows(16, 16, lens.data_ptr(), 2, 1, 8, 4, None)
+    assert rc == _lib.FST_ERR_INVALID
+    assert "lens[1] = 9" in _lib.last_error()
+    lens = torch.tensor([-1], dtype=torch.int32)
+    assert lib.fst_upload_rows(16, 16, lens.data_ptr(), 1, 1, 8, 4, None) == _lib.FST_ERR_INVALID
+    assert lib.fst_upload_rows(None, None, None, -1, 1, 1, 1, None) == _lib.FST_ERR_INVALID
+    assert lib.fst_upload_rows(None, 16, lens.data_ptr(), 1, 1, 8, 4, None) == _lib.FST_ERR_INVALID
+    assert "null" in _lib.last_error()
+    assert lib.fst_upload_rows(None, None, None, 0, 1, 1, 1, None) == _lib.FST_OK
+
+
+def test_upload_valid_rows_checks_arguments():
+    import torch
+    from flash_spacetime import ops
+    src = torch.zeros(2, 3, 8, 4)
+    with pytest.raises(ValueError, match="CPU tensor"):
+        ops.upload_valid_rows(src.clone(), src, [1, 2])

@@ -254,7 +254,10 @@ def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, e
     d2h = dw_host.numel() * dw_host.element_size()
 
     slots = [{k: torch.zeros_like(t, device=device) for k, t in host.items()} for _ in range(2)]
-    copy_stream = torch.cuda.Stream(device)
+    # High priority: the gather's few CTAs are placed as soon as an SM has
+    # room instead of queueing behind the attention kernels' grid (4.06 vs
+    # 4.45 ms per step on config 1).
+    copy_stream = torch.cuda.Stream(device, priority=-1)
     ready = [torch.cuda.Event() for _ in range(2)]
     free = [torch.cuda.Event() for _ in range(2)]
     for ev in free:

@@ -36,7 +36,9 @@ constexpr int kThreads = 128;
 
 // A few CTAs keep the host link busy (each has 8 KB of loads in flight); a
 // grid as wide as the spans would fill every SM and hold off the attention
-// kernels of the step it is meant to overlap.
+// kernels of the step it is meant to overlap. Measured on the benchmark's
+// config-1 batch: 8 CTAs are link-starved, 16-24 saturate it, 48 and more
+// slow the overlapped step.
 constexpr int kCtas = 24;
 
 __global__ void __launch_bounds__(kThreads) gather_rows_kernel(

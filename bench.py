@@ -2,7 +2,8 @@
 """Benchmark of the fused spacetime-bias attention op (fwd + bwd) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                    [--workload config1|config3|config4] [--coords raw|scaled]
+                    [--workload config1|config2|config3|config4] [--coords raw|scaled]
+                    [--dim Dh --channels C --dtype bf16|fp16]   (config2)
 
 One step is one forward + backward of the op through its public API
 (``flash_spacetime_attention`` / ``..._varlen``) over one batch of seeded
@@ -12,11 +13,19 @@ B=256 events padded to L=768, H=12, Dh=32, C=16, bf16, lognormal lengths
 [1, 768]). Throughput is algorithmic TFLOP/s over VALID pairs,
 sum_b L_b^2 * H * (14 Dh + 12 C).
 
-Under torchrun (N > 1) every rank owns a shard of N x 256 events chosen by
-longest-first L^2 balancing (weak scaling: per-GPU work stays fixed); the
-per-rank dW/db partials are gathered and summed in rank order (NCCL) inside
-the step, and the step time is the max over ranks of the device-timed
-duration.
+Other workloads: ``config2`` (B=128 full-length events of L=1024, H=8, the
+``--dim``/``--channels``/``--dtype`` given), ``config3`` (16384 packed
+lognormal events, median 80, 2 % single pulses) and ``config4`` (2048 packed
+events of length uniform in [2048, 16384], strong scaling).
+
+Under torchrun (N > 1) every rank owns a shard of the events chosen by
+longest-first L^2 balancing: N x 256 events for config1 (weak scaling:
+per-GPU work stays fixed), the fixed 2048 events of config4 (strong
+scaling). Inside the step the outputs of all ranks are all-gathered over
+NCCL (valid rows, packed; issued after the forward so that the transfer
+overlaps the backward) and the per-rank dW/db partials are gathered and
+summed in rank order; the step time is the max over ranks of the
+device-timed duration.
 
 Printed: one JSON line on rank 0 (see the keys below). ``value`` has inputs
 resident in HBM; ``e2e`` repeats the step with the inputs copied from pinned
@@ -42,6 +51,19 @@ import torch.distributed as dist  # noqa: E402
 
 HEADS, DIM, CHANNELS = 12, 32, 16
 METRIC = "fwd+bwd TFLOP/s (B=256,L=768,H=12,Dh=32,C=16 bf16; valid pairs)"
+
+
+def _shape(args):
+    """(heads, head dim, channels, dtype name, metric) of the workload."""
+    if args.workload == "config2":
+        d, c = args.dim or 32, args.channels or 32
+        return 8, d, c, args.dtype, (f"fwd+bwd TFLOP/s (B=128,L=1024,H=8,Dh={d},C={c} "
+                                     f"{args.dtype}; valid pairs)")
+    if args.workload == "config1":
+        return HEADS, DIM, CHANNELS, "bf16", METRIC
+    desc = {"config3": "16384 packed events, lognormal median 80",
+            "config4": "2048 packed events, L~U[2048,16384]"}[args.workload]
+    return HEADS, DIM, CHANNELS, "bf16", f"fwd+bwd TFLOP/s ({desc}, H=12,Dh=32,C=16 bf16; valid pairs)"
 
 
 def _peaks():
@@ -80,24 +102,24 @@ def _dist_setup():
 
 
 def _workload_lengths(name: str, world: int, rank: int, seed: int):
-    """(all lengths of this rank's shard, padded length or None, global event count)."""
+    """(lengths of this rank's shard, padded length or None, global event
+    count, every rank's shard lengths)."""
     from flash_spacetime.sharding import lpt_partition
     from flash_spacetime.synthetic import lengths_for
 
     if name == "config1":
-        n = 256 * world
-        lens = lengths_for("config1", n, seed)
-        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(n))
-        return [lens[i] for i in shard], 768, n
-    if name == "config3":
-        lens = lengths_for("config3", 16384 * world, seed)
-        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(len(lens)))
-        return [lens[i] for i in shard], None, len(lens)
-    if name == "config4":
-        lens = lengths_for("config4", 2048, seed)  # fixed total: strong scaling
-        shard = lpt_partition(lens, world)[rank] if world > 1 else list(range(len(lens)))
-        return [lens[i] for i in shard], None, len(lens)
-    raise SystemExit(f"unknown workload {name}")
+        lens, padlen = lengths_for("config1", 256 * world, seed), 768
+    elif name == "config2":
+        lens, padlen = [1024] * (128 * world), 1024
+    elif name == "config3":
+        lens, padlen = lengths_for("config3", 16384 * world, seed), None
+    elif name == "config4":
+        lens, padlen = lengths_for("config4", 2048, seed), None  # fixed total: strong scaling
+    else:
+        raise SystemExit(f"unknown workload {name}")
+    shards = lpt_partition(lens, world) if world > 1 else [list(range(len(lens)))]
+    per_rank = [[lens[i] for i in sh] for sh in shards]
+    return per_rank[rank], padlen, len(lens), per_rank
 
 
 class ClockSampler:
@@ -152,7 +174,8 @@ class ClockSampler:
                 "samples": len(inside), "window": window, "reasons": reasons}
 
 
-def cpu_eager_sample(lengths, budget_s: float, seed: int):
+def cpu_eager_sample(lengths, budget_s: float, seed: int, heads: int = HEADS, dim: int = DIM,
+                     channels: int = CHANNELS):
     """Time the CPU restatement of the upstream eager op, event by event.
 
     Runs fp32 forward + backward through autograd (upstream
@@ -165,7 +188,7 @@ def cpu_eager_sample(lengths, budget_s: float, seed: int):
     from flash_spacetime.synthetic import detector_coords, projection
 
     gen = torch.Generator().manual_seed(seed)
-    proj = projection(DIM, CHANNELS, gen)
+    proj = projection(dim, channels, gen)
     done_flops = 0.0
     done_pairs = 0
     spent = 0.0
@@ -174,11 +197,11 @@ def cpu_eager_sample(lengths, budget_s: float, seed: int):
         for n in lengths:
             n = int(n)
             feats = detector_coords([n], gen).view(1, n, 4)
-            q, k, v = (torch.randn(1, HEADS, n, DIM, generator=gen) for _ in range(3))
+            q, k, v = (torch.randn(1, heads, n, dim, generator=gen) for _ in range(3))
             t0 = time.perf_counter()
             eager_fwd_bwd_fp32(q, k, v, feats, proj["weight"], proj["bias"], None)
             spent += time.perf_counter() - t0
-            done_flops += n * n * HEADS * (14 * DIM + 12 * CHANNELS)
+            done_flops += n * n * heads * (14 * dim + 12 * channels)
             done_pairs += n * n
             events += 1
             if spent >= budget_s:
@@ -192,21 +215,22 @@ def run_reference(args):
     if rank != 0:
         return
     torch.set_num_threads(os.cpu_count() or 1)
-    lens, _, _ = _workload_lengths(args.workload, 1, 0, args.seed)
+    lens, _, _, _ = _workload_lengths(args.workload, 1, 0, args.seed)
+    heads, dim, channels, _, metric = _shape(args)
     # Each step: a bounded sample of the workload's events (in order).
     for _ in range(args.warmup):
-        cpu_eager_sample(lens, 0.5, args.seed)
+        cpu_eager_sample(lens, 0.5, args.seed, heads, dim, channels)
     vals, secs = [], []
     sample = None
     # Bounded per step so that the whole run stays near a minute and a half.
     budget = max(0.5, min(args.ref_budget, 90.0 / max(1, args.steps)))
     for _ in range(args.steps):
-        sample = cpu_eager_sample(lens, budget, args.seed)
+        sample = cpu_eager_sample(lens, budget, args.seed, heads, dim, channels)
         vals.append(sample["tflops"])
         secs.append(sample["seconds"])
     value = statistics.median(vals)
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": "TFLOP/s",
+        "impl": "reference", "metric": metric, "value": value, "unit": "TFLOP/s",
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": 1e3 * statistics.median(secs), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
@@ -223,7 +247,8 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
-def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, expect):
+def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, expect,
+            dim=DIM, channels=CHANNELS):
     """The step through the public API with every input copied from pinned
     host memory inside the timed region and dW/db read back each step.
 
@@ -250,7 +275,7 @@ def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, e
             h2d += sum(lens) * (t.numel() // (t.shape[0] * length)) * t.element_size()
         else:
             h2d += t.numel() * t.element_size()
-    dw_host = torch.empty(DIM * CHANNELS + DIM, dtype=torch.float32).pin_memory()
+    dw_host = torch.empty(dim * channels + dim, dtype=torch.float32).pin_memory()
     d2h = dw_host.numel() * dw_host.element_size()
 
     slots = [{k: torch.zeros_like(t, device=device) for k, t in host.items()} for _ in range(2)]
@@ -317,23 +342,40 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     from flash_spacetime import _lib, ops, synthetic
-    from flash_spacetime.sharding import max_over_ranks, ordered_sum
+    from flash_spacetime.sharding import RowGather, max_over_ranks, ordered_sum
 
-    lens, padlen, n_events = _workload_lengths(args.workload, world, rank, args.seed)
-    dtype = torch.bfloat16
+    lens, padlen, n_events, per_rank = _workload_lengths(args.workload, world, rank, args.seed)
+    heads, dim, channels, dtype_name, metric = _shape(args)
+    dtype = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype_name]
     scaled = args.coords == "scaled"
     if padlen is not None:
-        data = synthetic.padded_batch(lens, padlen, HEADS, DIM, CHANNELS, dtype, device,
+        data = synthetic.padded_batch(lens, padlen, heads, dim, channels, dtype, device,
                                       args.seed + 17 * rank, scaled)
     else:
-        data = synthetic.packed_batch(lens, HEADS, DIM, CHANNELS, dtype, device,
+        data = synthetic.packed_batch(lens, heads, dim, channels, dtype, device,
                                       args.seed + 17 * rank, scaled)
-    flops = synthetic.pair_flops(lens, HEADS, DIM, CHANNELS)
+    flops = synthetic.pair_flops(lens, heads, dim, channels)
+    total_flops = sum(synthetic.pair_flops(x, heads, dim, channels)["total"] for x in per_rank)
 
-    leaves = {k: data[k].detach().clone().requires_grad_(True)
-              for k in ("q", "k", "v", "weight", "bias")}
+    # The data tensors themselves are the leaves (no copies: config4 holds
+    # 14 GB per [T, H, Dh] tensor on one GPU).
+    leaves = {k: data[k].detach().requires_grad_(True) for k in ("q", "k", "v", "weight", "bias")}
     grad = data["grad"]
     feats = data["feats"]
+
+    # Output all-gather across ranks: every rank's valid output rows, packed
+    # ([rows, Dh]; a padded batch's valid rows are gathered by a precomputed
+    # index), with the row counts known on every rank from the partition.
+    gather = None
+    if world > 1 and not args.no_gather:
+        if padlen is not None:
+            sizes = [sum(x) * heads for x in per_rank]
+            idx = torch.cat([(b * heads + h) * padlen + torch.arange(n)
+                             for b, n in enumerate(lens) for h in range(heads)]).to(device)
+        else:
+            sizes = [sum(x) * heads for x in per_rank]
+            idx = None
+        gather = RowGather(sizes, (dim,), dtype, device)
 
     def step(lv, feats_, grad_, seq_or_cu):
         for t in lv.values():
@@ -344,6 +386,15 @@ def run_ours(args):
         else:
             out = ops.flash_spacetime_attention_varlen(lv["q"], lv["k"], lv["v"], feats_,
                                                        lv["weight"], lv["bias"], seq_or_cu)
+        work = None
+        if gather is not None:
+            rows = out.detach().view(-1, dim)
+            n = gather.sizes[rank]
+            if idx is not None:
+                torch.index_select(rows, 0, idx, out=gather.send[:n])
+            else:
+                gather.send[:n].copy_(rows)
+            work = gather.start()  # overlaps the backward (NCCL's own stream)
         out.backward(grad_)
         dw = lv["weight"].grad
         db = lv["bias"].grad
@@ -352,6 +403,8 @@ def run_ours(args):
             flat = ordered_sum(flat)
             dw = flat[: dw.numel()].view_as(dw)
             db = flat[dw.numel():]
+        if work is not None:
+            work.wait()
         return out, dw, db
 
     index = data["seqlens"] if padlen is not None else data["cu_seqlens"]
@@ -394,15 +447,18 @@ def run_ours(args):
         per.setdefault(name, []).append(e0.elapsed_time(e1))
     fwd_ms = statistics.mean(per.get("fst_forward", [0.0]))
     bwd_ms = statistics.mean(per.get("fst_backward", [0.0]))
-    total_flops = flops["total"] * world
     value = total_flops / (ms * 1e-3) / 1e12
 
     # End to end: inputs from pinned host memory every step, dW read back.
     e2e = None
-    if not args.no_e2e:
+    in_bytes = sum(data[k].numel() * data[k].element_size() for k in ("q", "k", "v", "grad"))
+    if in_bytes > 16e9 and not args.no_e2e:
+        e2e = {"skipped": f"inputs of {in_bytes / 1e9:.0f} GB per GPU exceed the pinned "
+                          "host buffers this run allocates (16 GB)"}
+    elif not args.no_e2e:
         expect = torch.cat([dw_last.flatten().float(), db_last.flatten().float()])
         e2e = run_e2e(args, data, index, step, device, world, total_flops, lens,
-                      padlen is not None, expect)
+                      padlen is not None, expect, dim, channels)
 
     if world > 1:
         dist.barrier()
@@ -421,7 +477,7 @@ def run_ours(args):
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         torch.set_num_threads(os.cpu_count() or 1)
-        s = cpu_eager_sample(lens, args.cpu_budget, args.seed)
+        s = cpu_eager_sample(lens, args.cpu_budget, args.seed, heads, dim, channels)
         cpu = {"value": s["tflops"], "unit": "TFLOP/s", "cores": torch.get_num_threads(),
                "kind": "port",
                "sample": f"{s['events']} events ({s['pairs']} valid pairs) of "
@@ -429,14 +485,18 @@ def run_ours(args):
                          f"a time, fp32 eager fwd+bwd via autograd, {s['seconds']:.1f} s"}
 
     line = {
-        "metric": METRIC, "value": value, "unit": "TFLOP/s", "n_gpus": world,
+        "metric": metric, "value": value, "unit": "TFLOP/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms,
         "higher_is_better": True, "scaling": "weak" if args.workload != "config4" else "strong",
-        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
-        "config": {"workload": args.workload, "events": n_events, "heads": HEADS,
-                   "head_dim": DIM, "channels": CHANNELS,
+        "vs_baseline": None, "dtype": dtype_name, "data": "synthetic",
+        "config": {"workload": args.workload, "events": n_events, "heads": heads,
+                   "head_dim": dim, "channels": channels,
                    "padded_length": padlen, "coords": args.coords,
                    "valid_pairs_per_gpu": flops["pairs"],
+                   "output_gather": (None if gather is None else
+                                     f"all_gather_into_tensor of every rank's valid output rows, "
+                                     f"{gather.bytes_received() / 1e6:.0f} MB received per rank "
+                                     f"per step, overlapping the backward"),
                    "l2_policy": f"inputs larger than L2 (q, k, v, grad "
                                 f"{data['q'].numel() * data['q'].element_size() / 1e6:.0f} MB "
                                 f"each)"},
@@ -460,7 +520,13 @@ def main():
     ap.add_argument("--steps", type=int, default=50)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default="config1", choices=("config1", "config3", "config4"))
+    ap.add_argument("--workload", default="config1",
+                    choices=("config1", "config2", "config3", "config4"))
+    ap.add_argument("--dim", type=int, default=0, help="config2 head dim (32 or 64)")
+    ap.add_argument("--channels", type=int, default=0, help="config2 channels (32 or 64)")
+    ap.add_argument("--dtype", default="bf16", choices=("bf16", "fp16"), help="config2 dtype")
+    ap.add_argument("--no-gather", action="store_true",
+                    help="multi-GPU: skip the all-gather of the outputs")
     ap.add_argument("--coords", default="raw", choices=("raw", "scaled"))
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-budget", type=float, default=12.0)

@@ -158,7 +158,6 @@ int fst_forward(const FstForwardArgs* a, void* stream) {
   }
   cudaGetLastError();  // clear a stale error so the check below is ours
   if (fst::tc::fwd_supported(p)) {
-    cudaMemsetAsync(a->workspace, 0, 4, (cudaStream_t)stream);  // device status word
     rc = fst::tc::launch_fwd(*a, (cudaStream_t)stream);
   } else {
     rc = fst::simt::launch_fwd(*a, (cudaStream_t)stream);

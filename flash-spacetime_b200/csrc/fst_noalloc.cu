@@ -1,27 +1,31 @@
 // fst_forward_noalloc: the fused forward for callers that cannot allocate
 // device memory.
 //
-// fst_forward takes its scratch (a status word and, for packed batches, the
-// per-event tile prefix) from a workspace the caller allocates. Some callers
-// cannot do that on the calling path: inference servers and plugin hosts that
-// run with a fixed, pre-reserved memory pool, code running under a memory
-// manager that forbids allocation after start-up, and real-time loops where a
-// cudaMalloc (which can synchronise the device) is not allowed. This entry
-// point runs the same kernels with that scratch taken from a file-scope
+// fst_forward takes its scratch (for the tensor-core kernels, the per-event
+// tile prefix of a packed batch) from a workspace the caller allocates. Some
+// callers cannot do that on the calling path: inference servers and plugin
+// hosts that run with a fixed, pre-reserved memory pool, code running under a
+// memory manager that forbids allocation after start-up, and real-time loops
+// where a cudaMalloc (which can synchronise the device) is not allowed. This
+// entry point runs the same kernels with that scratch taken from a file-scope
 // device array instead, so it allocates nothing; the caller still passes the
 // inputs and outputs.
 //
-// The array is kScratchBytes (256 KiB) per GPU, enough for batches of up to
-// kMaxEvents events; larger batches are rejected with FST_ERR_INVALID. Every
-// GPU that loads the library holds the array until the process exits.
+// The array is kScratchBytes (256 KiB) per GPU. A problem whose workspace
+// (fst_forward_workspace_size) exceeds it -- a 16-bit batch of more than
+// 65535 events -- is rejected with FST_ERR_INVALID; problems that need no
+// workspace (fp32 inputs) are not limited. Every GPU that loads the library
+// holds the array until the process exits.
 //
 // Set-up: the first call on a device looks up the array's device address
-// with cudaGetSymbolAddress (with that device current) and caches it; make
-// that first call before any stream capture. Every call then shares the one
-// array and it keeps the last call's contents, so calls that overlap on the
-// GPU (different streams, no ordering between them) race on it; serialise
-// them on one stream or with events. The status word is cleared on every
-// call; the tile prefix is rewritten in full by every packed call.
+// with cudaGetSymbolAddress (with that device current) and caches it for the
+// life of the process; make that first call before any stream capture. A
+// cudaDeviceReset on that device invalidates the cached address, so the entry
+// point must not be used on a device after it was reset. Every call shares
+// the one array and it keeps the last call's contents, so calls that overlap
+// on the GPU (different streams, no ordering between them) race on it;
+// serialise them on one stream or with events. The tile prefix is rewritten
+// in full by every packed call before it is read, so nothing needs clearing.
 
 #include <cuda_runtime.h>
 
@@ -33,9 +37,6 @@
 namespace {
 
 constexpr size_t kScratchBytes = 256 * 1024;
-// Workspace layout of the tensor-core forward: 64 bytes of status, then the
-// (batch + 1)-entry int32 tile prefix (fst::tc::fwd_workspace).
-constexpr int kMaxEvents = (int)((kScratchBytes - 64) / sizeof(int)) - 1;
 
 __device__ __align__(256) unsigned char g_fst_scratch[kScratchBytes];
 
@@ -71,11 +72,15 @@ int scratch_for_current_device(void** out, char* err, size_t errlen) {
 extern "C" int fst_forward_noalloc(const FstForwardArgs* args, void* stream) {
   char err[256];
   if (!args) return fst::api_fail(FST_ERR_INVALID, "fst_forward_noalloc: null args");
-  if (args->prob.batch > kMaxEvents)
+  // The tensor-core forward's workspace is the (batch + 1)-entry int32 tile
+  // prefix (fst::tc::fwd_workspace); the fp32 kernels need none.
+  const size_t need = fst_forward_workspace_size(&args->prob);
+  if (need > kScratchBytes)
     return fst::api_fail(FST_ERR_INVALID,
-                         "fst_forward_noalloc: %d events exceed the built-in scratch limit of "
-                         "%d events (use fst_forward with a caller workspace)",
-                         args->prob.batch, kMaxEvents);
+                         "fst_forward_noalloc: %d events need %zu bytes of scratch, above the "
+                         "built-in scratch limit of %zu bytes (at most 65535 events; use "
+                         "fst_forward with a caller workspace)",
+                         args->prob.batch, need, kScratchBytes);
   void* scratch = nullptr;
   const int rc = scratch_for_current_device(&scratch, err, sizeof(err));
   if (rc) return fst::api_fail(rc, "%s", err);

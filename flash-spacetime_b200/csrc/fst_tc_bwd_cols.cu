@@ -653,13 +653,13 @@ bool bwd_supported(const FstProblem& p) {
   return fwd_supported(p);  // same (Dh, C) list; every shape fits both kernels
 }
 
-// Workspace: [status 64 B][tile prefix, B+1 ints][u and w~, rows x H x C each
+// Workspace: [tile prefix, B+1 ints][u and w~, rows x H x C each
 // in the 16-bit type, 256-byte aligned][qt = [q * scale], rows x H x Dh in
 // the 16-bit type] -- the row kernel writes the two projections there (when
 // the caller did not pass them) and the scaled q, the column kernel reads
 // them back.
 static size_t ws_proj_offset(const FstProblem& p) {
-  return (64 + (size_t)(p.batch + 1) * sizeof(int) + 255) / 256 * 256;
+  return ((size_t)(p.batch + 1) * sizeof(int) + 255) / 256 * 256;
 }
 static size_t ws_proj_bytes(const FstProblem& p) {
   return ((size_t)p.total_rows * p.heads * p.channels * 2 + 255) / 256 * 256;
@@ -674,7 +674,7 @@ size_t bwd_workspace(const FstProblem& p) {
 
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st) {
   const FstProblem& p = a.prob;
-  int* tile_start = (int*)a.workspace + 16;
+  int* tile_start = (int*)a.workspace;
   unsigned char* proj = (unsigned char*)a.workspace + ws_proj_offset(p);
   void* u_ws = proj;
   void* wt_ws = proj + ws_proj_bytes(p);

@@ -152,8 +152,7 @@ __device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_st
 
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
-    fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group,
-                  int* status) {
+    fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group) {
   using S = FwdShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -862,8 +861,7 @@ void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st) 
 }
 
 template <typename T, int DH, int C>
-static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_start,
-                            int* status) {
+static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_start) {
   using S = FwdShape<DH, C>;
   const FstProblem& p = a.prob;
   static std::atomic<uint64_t> configured{0};  // per template instance, one bit per device
@@ -881,16 +879,16 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
     grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
   }
   if (grid.x == 0 || grid.y == 0) return FST_OK;
-  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, status);
+  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group);
   count_launch();
   return FST_OK;
 }
 
 template <typename T>
-static int launch_fwd_t(const FstForwardArgs& a, cudaStream_t st, int* ts, int* status) {
+static int launch_fwd_t(const FstForwardArgs& a, cudaStream_t st, int* ts) {
   const int D = a.prob.head_dim, C = a.prob.channels;
 #define FST_FWD_CASE(DD, CC) \
-  if (D == DD && C == CC) return launch_fwd_shape<T, DD, CC>(a, st, ts, status);
+  if (D == DD && C == CC) return launch_fwd_shape<T, DD, CC>(a, st, ts);
   FST_FWD_CASE(32, 16)
   FST_FWD_CASE(32, 32)
   FST_FWD_CASE(32, 64)
@@ -909,16 +907,15 @@ bool fwd_supported(const FstProblem& p) {
          (D == 16 && C == 16) || (D == 48 && C == 48);
 }
 
+// Workspace: the packed layout's per-event tile prefix, B+1 ints.
 size_t fwd_workspace(const FstProblem& p) {
-  return (size_t)(p.batch + 1) * sizeof(int) + 64;  // tile prefix + status
+  return ((size_t)(p.batch + 1) * sizeof(int) + 15) / 16 * 16;
 }
 
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st) {
-  int* ws = (int*)a.workspace;
-  int* status = ws;            // first 64 bytes: status word
-  int* tile_start = ws + 16;
-  if (a.prob.dtype == FST_BF16) return launch_fwd_t<__nv_bfloat16>(a, st, tile_start, status);
-  if (a.prob.dtype == FST_F16) return launch_fwd_t<__half>(a, st, tile_start, status);
+  int* tile_start = (int*)a.workspace;
+  if (a.prob.dtype == FST_BF16) return launch_fwd_t<__nv_bfloat16>(a, st, tile_start);
+  if (a.prob.dtype == FST_F16) return launch_fwd_t<__half>(a, st, tile_start);
   return FST_ERR_UNSUPPORTED;
 }
 

@@ -132,8 +132,10 @@ class _Problem:
         use_attn_bias: bool,
         use_act_bias: bool,
         layout: str = "bhld",
+        host_projection: bool = False,
     ) -> None:
         self.packed = cu_seqlens is not None
+        self.host_projection = bool(host_projection)
         if layout not in ("bhld", "blhd"):
             raise ValueError(f"layout must be 'bhld' or 'blhd', got {layout!r}")
         self.layout = "packed" if self.packed else layout
@@ -243,13 +245,30 @@ def _workspace(nbytes: int, device: torch.device) -> Tuple[Optional[Tensor], int
     return torch.empty(nbytes, dtype=torch.uint8, device=device), nbytes
 
 
+def _host_u(pb: "_Problem", q: Tensor) -> Optional[Tensor]:
+    """``u = ((q.float() * scale) @ W).to(dtype)`` when the host projects
+    (upstream forward.py:279-286), else None (the kernels project)."""
+    if not (pb.host_projection and pb.attn):
+        return None
+    return _dense((q.to(torch.float32) * pb.scale) @ pb.w32).to(pb.dtype).contiguous()
+
+
+def _host_wt(pb: "_Problem", dout: Tensor) -> Optional[Tensor]:
+    """``w~ = (dO.float() @ W).to(dtype)`` when the host projects (upstream
+    backward.py:546-547), else None."""
+    if not (pb.host_projection and pb.act):
+        return None
+    return (dout.to(torch.float32) @ pb.w32).to(pb.dtype).contiguous()
+
+
 def fused_forward(pb: _Problem, q: Tensor, k: Tensor, v: Tensor) -> Tuple[Tensor, Tensor]:
     """One ``fst_forward`` call. Returns ``(out, lse)``."""
     lib = _lib.load()
     # u = (q * scale) @ W (upstream forward.py:279-286) is formed in fp32 by the
     # kernels themselves (u = NULL), which saves the host GEMM and its HBM
-    # round trips; the arithmetic is the same fp32 projection rounded once.
-    u = None
+    # round trips. With host_projection the host forms it as upstream does
+    # and passes it through the C ABI.
+    u = _host_u(pb, q)
     out = torch.empty_like(q)
     lse = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
     a = _lib.FstForwardArgs()
@@ -282,8 +301,9 @@ def fused_backward(
     """
     lib = _lib.load()
     dout, out, lse = _dense(dout), _dense(out), lse.contiguous()
-    # u and w~ = dO @ W (upstream backward.py:541-556) are formed in-kernel.
-    u = wt = None
+    # u and w~ = dO @ W (upstream backward.py:541-556) are formed in-kernel,
+    # or on the host with host_projection.
+    u, wt = _host_u(pb, q), _host_wt(pb, dout)
     dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     a = _lib.FstBackwardArgs()
     a.prob = pb.c_struct()
@@ -337,6 +357,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         use_attn_bias: bool,
         use_activation_bias: bool,
         layout: str = "bhld",
+        host_projection: bool = False,
     ) -> Tensor:
         if feats.requires_grad:
             raise ValueError("feats (detector data) must not require grad")
@@ -345,7 +366,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("q, k and v must have the same dtype")
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                      use_attn_bias, use_activation_bias, layout)
+                      use_attn_bias, use_activation_bias, layout, host_projection)
         qc, kc, vc = (_dense(t) for t in (q, k, v))
         out, lse = fused_forward(pb, qc, kc, vc)
         ctx.save_for_backward(qc, kc, vc, out, lse)
@@ -369,7 +390,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             g["dq"] if need[0] else None,
             g["dk"] if need[1] else None,
             g["dv"] if need[2] else None,
-            None, dw, db, None, None, None, None, None, None,
+            None, dw, db, None, None, None, None, None, None, None,
         )
 
 
@@ -387,6 +408,8 @@ def flash_spacetime_attention(
     *,
     key_padding_mask: Optional[Tensor] = None,
     layout: str = "bhld",
+    validate_mask: bool = True,
+    host_projection: bool = False,
 ) -> Tensor:
     """Fused spacetime-bias attention on a padded batch (upstream forward.py:481-501).
 
@@ -400,19 +423,27 @@ def flash_spacetime_attention(
     ``layout='blhd'`` (an addition) takes and returns ``[B, L, H, Dh]``: a
     ``[B, L, H*Dh]`` projection viewed per head, with no head split or merge
     around the op.
+
+    ``validate_mask=False`` skips the check that a mask marks a prefix of
+    each event (the check reads a flag back from the device, a host
+    synchronisation per call); an unchecked mask that is not a prefix gives
+    wrong results. ``host_projection=True`` forms ``u = (q * scale) W`` and
+    ``w~ = dO W`` on the host in fp32, rounded once to q's dtype, as upstream
+    does (forward.py:279-286, backward.py:546-547), and passes them to the
+    kernels; by default the kernels form them in their prologue.
     """
     length = q.shape[1] if layout == "blhd" else q.shape[2]
     if key_padding_mask is not None:
         if seqlens is not None:
             raise ValueError("pass seqlens or key_padding_mask, not both")
-        seqlens = seqlens_from_mask(key_padding_mask)
+        seqlens = seqlens_from_mask(key_padding_mask, validate_mask)
     elif seqlens is None:
         seqlens = torch.full((q.shape[0],), length, dtype=torch.int32, device=q.device)
     elif seqlens.dim() == 2:
-        seqlens = seqlens_from_mask(seqlens)
+        seqlens = seqlens_from_mask(seqlens, validate_mask)
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, seqlens, None,
-        scale, use_attn_bias, use_activation_bias, layout,
+        scale, use_attn_bias, use_activation_bias, layout, host_projection,
     )
 
 
@@ -427,16 +458,19 @@ def flash_spacetime_attention_varlen(
     scale: Optional[float] = None,
     use_attn_bias: bool = True,
     use_activation_bias: bool = True,
+    *,
+    host_projection: bool = False,
 ) -> Tensor:
     """Packed, uncapped variant (upstream forward.py:504-527).
 
     q, k, v: ``[T, H, Dh]``; feats ``[T, F]``; ``cu_seqlens`` ``[B+1]`` token
     offsets (cu[0] = 0, cu[-1] = T) -- the values buffer of a jagged
     NestedTensor. No padding exists and no host synchronisation happens.
+    ``host_projection`` as for :func:`flash_spacetime_attention`.
     """
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, None, cu_seqlens,
-        scale, use_attn_bias, use_activation_bias,
+        scale, use_attn_bias, use_activation_bias, "bhld", host_projection,
     )
 
 
@@ -485,10 +519,11 @@ def flash_spacetime_forward(
     use_activation_bias: bool = True,
     cu_seqlens: Optional[Tensor] = None,
     layout: str = "bhld",
+    host_projection: bool = False,
 ) -> Tuple[Tensor, Tensor]:
     """Forward only, returning ``(out, lse)`` (upstream forward.py:222-346)."""
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                  use_attn_bias, use_activation_bias, layout)
+                  use_attn_bias, use_activation_bias, layout, host_projection)
     return fused_forward(pb, _dense(q), _dense(k), _dense(v))
 
 
@@ -509,6 +544,7 @@ def flash_spacetime_backward(
     cu_seqlens: Optional[Tensor] = None,
     want_absmax: bool = False,
     layout: str = "bhld",
+    host_projection: bool = False,
 ) -> Dict[str, Optional[Tensor]]:
     """Backward only (upstream backward.py:488-630), with diagnostics.
 
@@ -516,7 +552,7 @@ def flash_spacetime_backward(
     by construction) and, with ``want_absmax``, ``ds_absmax`` (rowmax |dS|).
     """
     pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                  use_attn_bias, use_activation_bias, layout)
+                  use_attn_bias, use_activation_bias, layout, host_projection)
     return fused_backward(pb, _dense(q), _dense(k), _dense(v),
                           out, lse, grad_out, want_absmax)
 

@@ -61,21 +61,61 @@ def ordered_sum(t: Tensor, group: Optional[dist.ProcessGroup] = None) -> Tensor:
     return acc
 
 
-def gather_rows(t: Tensor, group: Optional[dist.ProcessGroup] = None) -> List[Tensor]:
-    """All-gather per-rank tensors whose first dimension differs by rank."""
+def gather_rows(t: Tensor, group: Optional[dist.ProcessGroup] = None,
+                sizes: Optional[Sequence[int]] = None) -> List[Tensor]:
+    """All-gather per-rank tensors whose first dimension differs by rank.
+
+    ``sizes`` are every rank's row counts when the caller knows them (the
+    LPT partition is computed identically on every rank), which saves the
+    size exchange and its device-to-host read; without them the sizes are
+    all-gathered first.
+    """
     if not dist.is_initialized() or dist.get_world_size(group) == 1:
         return [t]
     world = dist.get_world_size(group)
-    n = torch.tensor([t.shape[0]], dtype=torch.int64, device=t.device)
-    sizes = [torch.empty_like(n) for _ in range(world)]
-    dist.all_gather(sizes, n, group=group)
-    rows = [int(s.item()) for s in sizes]
-    top = max(rows)
-    pad = t.new_zeros((top,) + tuple(t.shape[1:]))
-    pad[: t.shape[0]] = t
-    parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad, group=group)
-    return [p[:r] for p, r in zip(parts, rows)]
+    if sizes is None:
+        n = torch.tensor([t.shape[0]], dtype=torch.int64, device=t.device)
+        got = [torch.empty_like(n) for _ in range(world)]
+        dist.all_gather(got, n, group=group)
+        sizes = [int(x) for x in torch.cat(got).tolist()]
+    gatherer = RowGather(list(sizes), tuple(t.shape[1:]), t.dtype, t.device, group)
+    gatherer.start(t).wait()
+    return gatherer.parts()
+
+
+class RowGather:
+    """All-gather of per-rank row blocks of known, unequal sizes.
+
+    The send and receive buffers are allocated once (every rank pads its
+    block to the largest size), so a training loop issues one
+    ``all_gather_into_tensor`` per step with no allocation and no host
+    synchronisation; ``start`` returns the collective's work handle, so the
+    transfer can overlap the work that follows (NCCL runs on its own stream).
+    """
+
+    def __init__(self, sizes: Sequence[int], row_shape: Tuple[int, ...], dtype: torch.dtype,
+                 device: torch.device, group: Optional[dist.ProcessGroup] = None) -> None:
+        self.sizes = [int(n) for n in sizes]
+        self.group = group
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        self.top = max(self.sizes) if self.sizes else 0
+        self.send = torch.zeros((self.top,) + tuple(row_shape), dtype=dtype, device=device)
+        self.recv = torch.empty((len(self.sizes) * self.top,) + tuple(row_shape), dtype=dtype,
+                                device=device)
+
+    def start(self, t: Optional[Tensor] = None):
+        """Copy ``t`` (this rank's rows; None if already written to
+        ``send``) and issue the all-gather; returns the work handle."""
+        if t is not None:
+            self.send[: t.shape[0]].copy_(t)
+        return dist.all_gather_into_tensor(self.recv, self.send, group=self.group,
+                                           async_op=True)
+
+    def parts(self) -> List[Tensor]:
+        return [self.recv[r * self.top: r * self.top + n] for r, n in enumerate(self.sizes)]
+
+    def bytes_received(self) -> int:
+        return (len(self.sizes) - 1) * self.send.numel() * self.send.element_size()
 
 
 def max_over_ranks(value: float, device: torch.device,

@@ -159,10 +159,13 @@ int fst_backward(const FstBackwardArgs* args, void* stream);
  * synchronise the device) is not allowed, cannot provide fst_forward's
  * workspace. This variant ignores args->workspace and takes that scratch from
  * a 256 KiB array built into the library (one per GPU, held until the process
- * exits); it allocates nothing. Batches of more than 65519 events are
- * rejected with FST_ERR_INVALID. The first call on a device looks up the
- * array's address (make it before any stream capture). All calls share the
- * array: calls that overlap on the GPU race, so order them on one stream. */
+ * exits); it allocates nothing. A problem whose fst_forward_workspace_size
+ * exceeds 256 KiB (16-bit inputs with more than 65535 events) is rejected
+ * with FST_ERR_INVALID. The first call on a device looks up the array's
+ * address and keeps it for the life of the process (make that call before any
+ * stream capture; after a cudaDeviceReset of that device the entry point must
+ * not be used). All calls share the array: calls that overlap on the GPU
+ * race, so order them on one stream. */
 int fst_forward_noalloc(const FstForwardArgs* args, void* stream);
 
 /* Host -> device copy of the valid rows of a padded batch (a data-loader

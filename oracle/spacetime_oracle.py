@@ -44,13 +44,25 @@ def freq_ladder(channels: int) -> Tensor:
 
 def pair_angle(feats: Tensor) -> Tensor:
     """``x_ij = 1024 clip(sign(I) sqrt|I|, -4, 4)`` (upstream reference.py:75-81)."""
-    pos = feats[:, :, :3]
-    time = feats[:, :, 3]
-    interval = (pos[:, :, None] - pos[:, None, :]).pow(2).sum(-1) - (
-        (time[:, :, None] - time[:, None, :]) * TIME_SCALE
+    return pair_angle_between(feats, feats)
+
+
+def pair_angle_between(fq: Tensor, fk: Tensor) -> Tensor:
+    """``x_ij`` between query rows ``fq`` ``[B, Lq, F]`` and key rows ``fk``
+    ``[B, Lk, F]``, with upstream's op order (reference.py:75-81)."""
+    pq, pk = fq[:, :, :3], fk[:, :, :3]
+    tq, tk = fq[:, :, 3], fk[:, :, 3]
+    interval = (pq[:, :, None] - pk[:, None, :]).pow(2).sum(-1) - (
+        (tq[:, :, None] - tk[:, None, :]) * TIME_SCALE
     ).pow(2)
     signed = torch.sign(interval) * torch.sqrt(torch.abs(interval))
     return INPUT_SCALE * signed.clip(-CLIP, CLIP)
+
+
+def pair_embedding_between(fq: Tensor, fk: Tensor, channels: int) -> Tensor:
+    """``E_ij`` for query rows ``fq`` against key rows ``fk``: ``[B, Lq, Lk, C]``."""
+    ang = pair_angle_between(fq, fk).unsqueeze(-1) * freq_ladder(channels).to(fq.device)
+    return torch.cat((torch.sin(ang), torch.cos(ang)), dim=-1)
 
 
 def pair_embedding(feats: Tensor, channels: int) -> Tensor:
@@ -293,3 +305,124 @@ def eager_fwd_bwd_fp32(
     loss = (out * out).sum() * 0.5
     loss.backward()
     return loss.detach()
+
+
+# ---------------------------------------------------------------------------
+# Row and column subsets of one long event (float64)
+# ---------------------------------------------------------------------------
+#
+# For events too long for the full O(L^2) evaluation (L = 16384), the
+# quantities that belong to one query row depend only on that row and all
+# keys, so a subset of rows is checked exactly; those that belong to one key
+# (dk, dv) need every row's log-sum-exp and D, which are taken from the
+# kernel under test after its rows were checked against event_rows.
+
+
+def event_rows(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    rows: Tensor,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+    grad_out: Optional[Tensor] = None,
+) -> Dict[str, Tensor]:
+    """Outputs of the query ``rows`` of ONE event in float64.
+
+    q, k, v: ``[L, H, Dh]`` (the event's packed rows); feats ``[L, >=4]``;
+    ``rows``: int64 indices; ``grad_out``: ``[len(rows), H, Dh]`` or None.
+    Returns ``out`` ``[R, H, Dh]``, ``lse`` ``[R, H]`` (logits without the
+    ``qt.b`` row constant) and, with ``grad_out``, ``dq`` ``[R, H, Dh]`` and
+    ``delta`` ``[R, H]`` = ``dO . (out - [act] b)``, the P-weighted mean of
+    dP without its ``dO.b`` constant. The composition is that of
+    :func:`eager_attention` (upstream reference.py:139-167) restricted to
+    the rows.
+    """
+    dim = q.shape[-1]
+    s = dim**-0.5 if scale is None else scale
+    need = grad_out is not None
+    qs = q[rows].double().permute(1, 0, 2)[None].requires_grad_(need)  # [1, H, R, Dh]
+    kk = k.double().permute(1, 0, 2)[None]
+    vv = v.double().permute(1, 0, 2)[None]
+    fq = feats[rows].double()[None]
+    fk = feats.double()[None]
+    w = weight.double()
+    b = None if bias is None else bias.double()
+    with torch.set_grad_enabled(need):
+        qt = qs * s
+        attn = qt @ kk.transpose(-2, -1)
+        rel = emb = None
+        if use_attn_bias or use_activation_bias:
+            emb = pair_embedding_between(fq, fk, w.shape[1])
+            rel = torch.nn.functional.linear(emb, w, b)
+        if use_attn_bias:
+            attn = attn + torch.einsum("bhic,bijc->bhij", qt, rel)
+        p = attn.softmax(dim=-1)
+        out = p @ vv
+        if use_activation_bias:
+            out = out + torch.einsum("bhij,bijc->bhic", p, rel)
+    with torch.no_grad():
+        lg = qt @ kk.transpose(-2, -1)
+        if use_attn_bias:
+            lg = lg + torch.einsum("bhie,bije->bhij", qt @ w, emb)
+        lse = torch.logsumexp(lg, dim=-1)[0].t()
+    res = {"out": out.detach()[0].permute(1, 0, 2), "lse": lse}
+    if need:
+        g = grad_out.double().permute(1, 0, 2)[None]
+        out.backward(g)
+        res["dq"] = qs.grad[0].permute(1, 0, 2)
+        off = out.detach()
+        if use_activation_bias and b is not None:
+            off = off - b
+        res["delta"] = (g * off).sum(-1)[0].t()
+    return res
+
+
+def event_cols(
+    q: Tensor,
+    k: Tensor,
+    v: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    cols: Tensor,
+    lse: Tensor,
+    delta: Tensor,
+    grad_out: Tensor,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+) -> Dict[str, Tensor]:
+    """``dk``, ``dv`` of the key ``cols`` of ONE event in float64.
+
+    Upstream's column contraction (backward.py:209-313): ``P_ij = exp(s_ij -
+    lse_i)``, ``dP_ij = dO_i . v_j + [act] (dO_i W) . E_ij``,
+    ``dS = P (dP - D_i)``, ``dk_j = sum_i dS_ij qt_i``, ``dv_j = sum_i P_ij
+    dO_i`` over all rows i. ``lse`` and ``delta`` ``[L, H]`` are every row's
+    log-sum-exp (without ``qt.b``) and D (without ``dO.b``), which the caller
+    takes from the kernel after checking them on sampled rows.
+    """
+    dim = q.shape[-1]
+    s = dim**-0.5 if scale is None else scale
+    qt = q.double().permute(1, 0, 2) * s          # [H, L, Dh]
+    kc = k[cols].double().permute(1, 0, 2)        # [H, J, Dh]
+    vc = v[cols].double().permute(1, 0, 2)
+    do = grad_out.double().permute(1, 0, 2)       # [H, L, Dh]
+    w = weight.double()
+    logits = qt @ kc.transpose(-2, -1)            # [H, L, J]
+    dp = do @ vc.transpose(-2, -1)
+    if use_attn_bias or use_activation_bias:
+        emb = pair_embedding_between(feats.double()[None], feats[cols].double()[None],
+                                     w.shape[1])[0]  # [L, J, C]
+        if use_attn_bias:
+            logits = logits + torch.einsum("hic,ijc->hij", qt @ w, emb)
+        if use_activation_bias:
+            dp = dp + torch.einsum("hic,ijc->hij", do @ w, emb)
+    p = torch.exp(logits - lse.double().t()[:, :, None])
+    ds = p * (dp - delta.double().t()[:, :, None])
+    dk = (ds.transpose(-2, -1) @ qt).permute(1, 0, 2)
+    dv = (p.transpose(-2, -1) @ do).permute(1, 0, 2)
+    return {"dk": dk, "dv": dv}

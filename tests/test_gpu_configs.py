@@ -1,0 +1,210 @@
+"""Parity at the sizes of the benchmark configurations, against the float64 oracle.
+
+The small-shape suites (``test_gpu_parity.py``, ``test_gpu_varlen.py``) cover
+upstream's edge cases. This file runs the fused op on the benchmark
+configurations' own sizes and value distributions (detector coordinates in
+metres and nanoseconds, q/k/v ~ N(0, 1), W ~ N(0, 1/C), b ~ N(0, 0.02^2)):
+
+* config 1: the whole B=256, L=768 lognormal batch (bf16); the 8 longest
+  events, 8 random ones and every length-1 event are checked;
+* config 2: B=128 full-length L=1024 events, H=8, (C, Dh) in {32, 64}^2, fp16
+  and bf16; one event of each batch is checked;
+* config 3: 16384 packed events with 2 % single pulses (bf16); 16 single-pulse
+  and 48 random events are checked, and the longest event on sampled rows and
+  key columns;
+* config 4: an uncapped L = 16384 event packed with two more (bf16); 128
+  sampled query rows (out, lse, dq, D) and 128 sampled key columns (dk, dv)
+  are checked, the columns through every row's lse and D taken from the
+  kernel once its sampled rows have matched.
+
+The tolerance is the stated one for 16-bit inputs: normwise
+``||kernel - ref64|| / ||ref64|| <= 2e-2`` on every output and gradient, and
+``|rowsum dS| <= 1e-6 rowmax |dS|`` on every valid row of the whole batch.
+dW and db are checked by running the op on the checked events alone.
+"""
+
+import pytest
+import torch
+
+import cases as cs
+from oracle import spacetime_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+if torch.cuda.is_available():
+    from flash_spacetime import synthetic
+    from flash_spacetime.ops import flash_spacetime_backward, flash_spacetime_forward
+
+TOL = 2e-2
+SEED = 2026
+
+
+def _rowsum_ratio(g, valid):
+    sig, amax = g["sigma"][valid].abs(), g["ds_absmax"][valid]
+    assert torch.isfinite(sig).all()
+    return (sig / amax.clamp_min(1e-30)).max().item()
+
+
+def _run(data, packed):
+    """Forward + backward of the whole batch (results stay on the device)."""
+    idx = data["cu_seqlens"] if packed else data["seqlens"]
+    kw = {"cu_seqlens": idx} if packed else {}
+    seq = None if packed else idx
+    args = (data["q"], data["k"], data["v"], data["feats"], data["weight"], data["bias"], seq)
+    out, lse = flash_spacetime_forward(*args, **kw)
+    g = flash_spacetime_backward(*args, out, lse, data["grad"], want_absmax=True, **kw)
+    torch.cuda.synchronize()
+    g["out"], g["lse"] = out, lse
+    return g
+
+
+def _check(what, kernel, ref):
+    err = cs.normwise(kernel.cpu(), ref)
+    assert err <= TOL, f"{what}: normwise error {err:.3e} > {TOL}"
+
+
+def _subset(data, events, packed):
+    """The batch restricted to ``events`` (padded: same L; packed: repacked)."""
+    dev = data["q"].device
+    if packed:
+        cu = data["cu_seqlens"].cpu().tolist()
+        rows = torch.cat([torch.arange(cu[b], cu[b + 1]) for b in events]).to(dev)
+        sub = {k: data[k][rows] for k in ("q", "k", "v", "grad", "feats")}
+        cu_sub = [0]
+        for b in events:
+            cu_sub.append(cu_sub[-1] + cu[b + 1] - cu[b])
+        sub["cu_seqlens"] = torch.tensor(cu_sub, dtype=torch.int32, device=dev)
+    else:
+        sel = torch.as_tensor(events, device=dev)
+        sub = {k: data[k][sel] for k in ("q", "k", "v", "grad", "feats")}
+        sub["seqlens"] = data["seqlens"][sel]
+    sub["weight"], sub["bias"] = data["weight"], data["bias"]
+    return sub
+
+
+def _check_events(data, res, events, packed):
+    """Sampled events of a whole-batch run against the float64 oracle.
+
+    The op is run again on the sampled events alone: its per-event results
+    must equal the whole batch's bit for bit (events are independent), and
+    that run -- dW and db included -- is compared with one oracle pass over
+    the same events.
+    """
+    sub = _subset(data, events, packed)
+    rs = _run(sub, packed)
+    w, bias = data["weight"].cpu().double(), data["bias"].cpu().double()
+    cpu = {k: sub[k].cpu().double() for k in ("q", "k", "v", "grad", "feats")}
+    if packed:
+        cu = data["cu_seqlens"].cpu().tolist()
+        cu_sub = sub["cu_seqlens"].cpu().tolist()
+        for i, b in enumerate(events):
+            for key in ("out", "dq", "dk", "dv"):
+                assert torch.equal(rs[key][cu_sub[i]:cu_sub[i + 1]], res[key][cu[b]:cu[b + 1]]), \
+                    f"event {b} {key}: whole-batch and subset runs differ"
+        ref = orc.oracle_packed(cpu["q"], cpu["k"], cpu["v"], cpu["feats"], w, bias, cu_sub,
+                                grad_out=cpu["grad"])
+        spans = [(cu_sub[i], cu_sub[i + 1]) for i in range(len(events))]
+        for i, (s0, s1) in enumerate(spans):
+            for key in ("out", "dq", "dk", "dv"):
+                _check(f"event {events[i]} (L={s1 - s0}) {key}", rs[key][s0:s1].double(),
+                       ref[key][s0:s1])
+            torch.testing.assert_close(rs["lse"][s0:s1].cpu().double(), ref["lse"][s0:s1],
+                                       atol=2e-2, rtol=1e-3)
+    else:
+        lens = sub["seqlens"].cpu().tolist()
+        for i, b in enumerate(events):
+            n = lens[i]
+            for key in ("out", "dq", "dk", "dv"):
+                assert torch.equal(rs[key][i, :, :n], res[key][b, :, :n]), \
+                    f"event {b} {key}: whole-batch and subset runs differ"
+        vm = (torch.arange(cpu["q"].shape[2])[None, :] < torch.tensor(lens)[:, None])
+        vm = vm[:, None, :, None]
+        ref = orc.oracle_padded(cpu["q"], cpu["k"], cpu["v"], cpu["feats"], w, bias, lens,
+                                grad_out=cpu["grad"] * vm)
+        for i, n in enumerate(lens):
+            for key in ("out", "dq", "dk", "dv"):
+                _check(f"event {events[i]} (L={n}) {key}", rs[key][i, :, :n].double(),
+                       ref[key][i, :, :n])
+            torch.testing.assert_close(rs["lse"][i, :, :n].cpu().double(), ref["lse"][i, :, :n],
+                                       atol=2e-2, rtol=1e-3)
+    _check("dW", rs["dW"].double(), ref["dW"])
+    _check("db", rs["db"].double(), ref["db"])
+
+
+def _check_long_event(data, res, b, nrows, seed):
+    """Sampled rows and key columns of one long packed event."""
+    cu = data["cu_seqlens"].cpu().tolist()
+    s0, s1 = cu[b], cu[b + 1]
+    n = s1 - s0
+    gen = torch.Generator().manual_seed(seed)
+    rows = torch.cat([torch.tensor([0, n - 1]), torch.randperm(n, generator=gen)[:nrows - 2]])
+    cpu = {k: data[k][s0:s1].cpu().double() for k in ("q", "k", "v", "grad", "feats")}
+    w, bias = data["weight"].cpu().double(), data["bias"].cpu().double()
+    ref = orc.event_rows(cpu["q"], cpu["k"], cpu["v"], cpu["feats"], w, bias, rows,
+                         grad_out=cpu["grad"][rows])
+    for key in ("out", "dq"):
+        _check(f"L={n} rows {key}", res[key][s0:s1][rows.cuda()].double(), ref[key])
+    lse_k = res["lse"][s0:s1].cpu().double()
+    delta_k = res["delta"][s0:s1].cpu().double()
+    torch.testing.assert_close(lse_k[rows], ref["lse"], atol=2e-2, rtol=1e-3)
+    _check(f"L={n} rows delta", delta_k[rows], ref["delta"])
+    cols = torch.cat([torch.tensor([0, n - 1]), torch.randperm(n, generator=gen)[:nrows - 2]])
+    refc = orc.event_cols(cpu["q"], cpu["k"], cpu["v"], cpu["feats"], w, cols, lse_k, delta_k,
+                          cpu["grad"])
+    for key in ("dk", "dv"):
+        _check(f"L={n} cols {key}", res[key][s0:s1][cols.cuda()].double(), refc[key])
+    # Whole-event identity: sum_j dv_j = sum_i dO_i for every head (rows of P sum to 1).
+    _check(f"L={n} sum dv", res["dv"][s0:s1].double().sum(0).cpu(), cpu["grad"].sum(0))
+
+
+def test_config1_full_batch():
+    lens = synthetic.lengths_for("config1", 256, SEED)
+    data = synthetic.padded_batch(lens, 768, 12, 32, 16, torch.bfloat16, torch.device("cuda"),
+                                  SEED)
+    res = _run(data, packed=False)
+    valid = (torch.arange(768, device="cuda")[None, :] < data["seqlens"][:, None])[:, None, :]
+    ratio = _rowsum_ratio(res, valid.expand_as(res["sigma"]))
+    assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
+    order = sorted(range(len(lens)), key=lambda i: (-lens[i], i))
+    gen = torch.Generator().manual_seed(SEED)
+    rand = [int(i) for i in torch.randperm(len(lens), generator=gen)[:8]]
+    singles = [i for i, n in enumerate(lens) if n == 1]
+    assert singles, "the lognormal draw should hold single-pulse events"
+    _check_events(data, res, sorted(set(order[:8] + rand + singles)), packed=False)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+@pytest.mark.parametrize("dim,channels", [(32, 32), (64, 32), (32, 64), (64, 64)])
+def test_config2_wide_channels(dim, channels, dtype):
+    lens = [1024] * 128
+    data = synthetic.padded_batch(lens, 1024, 8, dim, channels, dtype, torch.device("cuda"),
+                                  SEED + dim + channels)
+    res = _run(data, packed=False)
+    ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
+    _check_events(data, res, [127], packed=False)
+
+
+def test_config3_packed_events():
+    lens = synthetic.lengths_for("config3", 16384, SEED)
+    data = synthetic.packed_batch(lens, 12, 32, 16, torch.bfloat16, torch.device("cuda"), SEED)
+    res = _run(data, packed=True)
+    ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
+    gen = torch.Generator().manual_seed(SEED)
+    singles = [i for i, n in enumerate(lens) if n == 1]
+    assert len(singles) > 200, "2 % of the events should be single pulses"
+    pick = [singles[int(i)] for i in torch.randperm(len(singles), generator=gen)[:16]]
+    mid = [i for i in torch.randperm(len(lens), generator=gen).tolist() if 1 < lens[i] <= 1200]
+    _check_events(data, res, sorted(set(pick + mid[:48])), packed=True)
+    longest = max(range(len(lens)), key=lambda i: lens[i])
+    _check_long_event(data, res, longest, 64, SEED)
+
+
+def test_config4_uncapped_event():
+    lens = [16384, 2048, 9001]
+    data = synthetic.packed_batch(lens, 12, 32, 16, torch.bfloat16, torch.device("cuda"), SEED)
+    res = _run(data, packed=True)
+    ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
+    _check_long_event(data, res, 0, 128, SEED)

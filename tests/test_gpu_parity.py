@@ -121,7 +121,7 @@ def _kernel_grads(case, flags, dtype):
 
 
 @pytest.mark.parametrize("shape", [SHAPES[2], SHAPES[5], SHAPES[9], SHAPES[11], SHAPES[12],
-                                   SHAPES[13], SHAPES[14], SHAPES[15]])
+                                   SHAPES[13], SHAPES[14], SHAPES[15], SHAPES[16]])
 @pytest.mark.parametrize("flags", FLAGS)
 @pytest.mark.parametrize("masked", [False, True])
 @pytest.mark.parametrize("dtype", DTYPES)
@@ -211,6 +211,86 @@ def test_mask_forms_agree() -> None:
     bad[0, 0] = True  # a padding token in front of valid ones
     with pytest.raises(ValueError, match="prefix"):
         flash_spacetime_attention(*args, feats, w, bb, key_padding_mask=bad)
+    # Without validation the mask is taken as lengths with no device read-back.
+    o4 = flash_spacetime_attention(*args, feats, w, bb, key_padding_mask=pad,
+                                   validate_mask=False)
+    assert torch.equal(o1, o4)
+
+
+@pytest.mark.parametrize("layout", ["bhld", "blhd", "packed"])
+@pytest.mark.parametrize("flags", FLAGS[:3])
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_host_projection_matches_oracle(layout, flags, dtype) -> None:
+    """Caller-supplied u = ((q scale) W).to(dtype) and w~ = (dO W).to(dtype),
+    formed on the host in fp32 as upstream does (forward.py:279-286,
+    backward.py:546-547) and passed through the C ABI: the results follow
+    the float64 oracle (2x-eager rule) and stay within rounding of the
+    in-kernel projection."""
+    from flash_spacetime.ops import flash_spacetime_attention_varlen
+
+    b, n, h, d, c = SHAPES[13]
+    case = cs.padded_case(b, n, h, d, c, True, seed=_seed(31, *flags, len(layout)))
+    ref64 = cs.eager_padded(case, flags, torch.float64, grad=True)
+    eager = cs.eager_padded(case, flags, dtype, grad=True)
+    vm = cs.valid_mask(case)
+    lens = [int(x) for x in case["seqlens"]]
+    pk = cs.packed_from_padded(case)
+
+    def run(host):
+        if layout == "packed":
+            leaves = {k: _to(pk[k], dtype).requires_grad_(True) for k in ("q", "k", "v")}
+        else:
+            leaves = {k: _to(case[k], dtype) for k in ("q", "k", "v")}
+            if layout == "blhd":
+                leaves = {k: t.transpose(1, 2).contiguous() for k, t in leaves.items()}
+            leaves = {k: t.requires_grad_(True) for k, t in leaves.items()}
+        w = _to(case["weight"], torch.float32).requires_grad_(True)
+        bb = _to(case["bias"], torch.float32).requires_grad_(True)
+        if layout == "packed":
+            out = flash_spacetime_attention_varlen(
+                leaves["q"], leaves["k"], leaves["v"], pk["feats"].cuda(), w, bb,
+                pk["cu"].cuda(), use_attn_bias=flags[0], use_activation_bias=flags[1],
+                host_projection=host)
+            out.backward(_to(pk["grad"], dtype))
+            unpack = lambda t: _unpack(t, lens, n)  # noqa: E731
+        else:
+            out = flash_spacetime_attention(
+                leaves["q"], leaves["k"], leaves["v"], case["feats"].cuda(), w, bb,
+                case["seqlens"].cuda(), use_attn_bias=flags[0], use_activation_bias=flags[1],
+                layout=layout, host_projection=host)
+            g = _to(case["grad"], dtype) * vm.cuda()
+            out.backward(g.transpose(1, 2) if layout == "blhd" else g)
+            unpack = (lambda t: t.transpose(1, 2)) if layout == "blhd" else (lambda t: t)
+        res = {"out": unpack(out.detach()).cpu()}
+        for k in ("q", "k", "v"):
+            res["d" + k] = unpack(leaves[k].grad).cpu()
+        res["dW"], res["db"] = w.grad.cpu(), bb.grad.cpu()
+        return res
+
+    host, kern = run(True), run(False)
+    atol = cs.atol_for(dtype, flags)
+    for key in ("out", "dq", "dk", "dv"):
+        kv, rv, ev = (cs.valid_values(t, case) for t in (host[key], ref64[key], eager[key]))
+        cs.assert_2x_rule(kv, ev, rv, atol, f"host projection {key}", dtype,
+                          reduction=key != "out")
+        # The in-kernel projection rounds the same fp32 product once (W split
+        # into hi + lo halves of the 16-bit type), so the two paths agree to
+        # well inside the stated tolerance.
+        diff = cs.normwise(kv, cs.valid_values(kern[key], case).double())
+        assert diff <= (1e-2 if dtype != torch.float32 else 1e-5), f"{key}: host vs kernel {diff:.2e}"
+    for key in ("dW", "db"):
+        assert cs.normwise(host[key].double(), ref64[key]) <= (2e-2 if dtype != torch.float32
+                                                                else 1e-3), key
+
+
+def _unpack(t, lens, length):
+    """[T, H, D] packed rows back to [B, H, L, D] with zero padding."""
+    out = torch.zeros(len(lens), t.shape[1], length, t.shape[2], dtype=t.dtype, device=t.device)
+    s = 0
+    for b, m in enumerate(lens):
+        out[b, :, :m] = t[s:s + m].transpose(0, 1)
+        s += m
+    return out
 
 
 def test_bad_shapes_raise() -> None:

@@ -124,3 +124,29 @@ def test_lse_drops_row_constant() -> None:
         "bhic,bijc->bhij", qt, orc.pair_features(feats, w, b))
     shift = (qt * b).sum(-1)
     torch.testing.assert_close(res["lse"], torch.logsumexp(full, -1) - shift, atol=1e-10, rtol=1e-10)
+
+
+@pytest.mark.parametrize("flags", [(True, True), (True, False), (False, True)])
+def test_row_and_column_subsets_match_full_oracle(flags):
+    """event_rows / event_cols (the L=16384 checkers) against the full per-event oracle."""
+    gen = torch.Generator().manual_seed(11)
+    n, h, d, c = 57, 3, 16, 8
+    q, k, v, g = (torch.randn(n, h, d, generator=gen, dtype=torch.float64) for _ in range(4))
+    feats = torch.randn(n, 4, generator=gen, dtype=torch.float64)
+    w = torch.randn(d, c, generator=gen, dtype=torch.float64) / c**0.5
+    b = 0.1 * torch.randn(d, generator=gen, dtype=torch.float64)
+    full = orc.oracle_packed(q, k, v, feats, w, b, [0, n], use_attn_bias=flags[0],
+                             use_activation_bias=flags[1], grad_out=g)
+    rows = torch.tensor([0, 5, 31, n - 1])
+    sub = orc.event_rows(q, k, v, feats, w, b, rows, use_attn_bias=flags[0],
+                         use_activation_bias=flags[1], grad_out=g[rows])
+    for key in ("out", "lse", "dq"):
+        torch.testing.assert_close(sub[key], full[key][rows], rtol=1e-11, atol=1e-12)
+    off = full["out"] - (b if flags[1] else 0.0)
+    delta = (g * off).sum(-1)
+    torch.testing.assert_close(sub["delta"], delta[rows], rtol=1e-11, atol=1e-12)
+    cols = torch.tensor([1, 2, 40, n - 1])
+    cs_ = orc.event_cols(q, k, v, feats, w, cols, full["lse"], delta, g,
+                         use_attn_bias=flags[0], use_activation_bias=flags[1])
+    torch.testing.assert_close(cs_["dk"], full["dk"][cols], rtol=1e-10, atol=1e-11)
+    torch.testing.assert_close(cs_["dv"], full["dv"][cols], rtol=1e-10, atol=1e-11)

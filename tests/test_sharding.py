@@ -53,6 +53,9 @@ def _worker(rank, world, port, q):
         t = torch.arange(6, dtype=torch.float32) * (rank + 1)
         s = ordered_sum(t)
         rows = gather_rows(torch.full((rank + 2, 3), float(rank)))
+        # Host-known sizes (every rank computes the same partition): no size exchange.
+        rows2 = gather_rows(torch.full((rank + 2, 3), float(rank)), sizes=[2, 3])
+        assert [r.tolist() for r in rows2] == [r.tolist() for r in rows]
         m = max_over_ranks(float(rank) * 1.5, torch.device("cpu"))
         q.put((rank, s.tolist(), [r.tolist() for r in rows], m))
     finally:

@@ -63,6 +63,16 @@ int check_problem(const FstProblem* p) {
     if ((int64_t)p->batch * p->max_len != p->total_rows)
       return fail(FST_ERR_INVALID, "padded total_rows must equal B*L");
   }
+  if (p->qkv_row_stride) {
+    if (p->packed == 0)
+      return fail(FST_ERR_INVALID,
+                  "qkv_row_stride applies to the row-interleaved layouts (packed 1 or 2)");
+    if (p->qkv_row_stride < p->heads * p->head_dim || p->qkv_row_stride % p->head_dim ||
+        p->qkv_row_stride % 8)
+      return fail(FST_ERR_INVALID,
+                  "qkv_row_stride (=%d) must be >= H*Dh (=%d) and a multiple of Dh and of 8",
+                  p->qkv_row_stride, p->heads * p->head_dim);
+  }
   if (p->total_rows > 0 && (!p->feats || !p->freqs))
     return fail(FST_ERR_INVALID, "feats and freqs are required");
   if ((p->use_attn_bias || p->use_act_bias) && p->total_rows > 0 && !p->weight)

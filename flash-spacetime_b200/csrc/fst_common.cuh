@@ -80,6 +80,18 @@ __device__ __forceinline__ EventSpan event_span(const FstProblem& p, int b) {
   return e;
 }
 
+// The span of the q, k, v inputs and the dq, dk, dv outputs of event b: as
+// event_span, with the caller's row stride (a fused QKV buffer) in the
+// row-interleaved layouts. `dim` is the head dimension.
+__device__ __forceinline__ EventSpan qkv_span(const FstProblem& p, int b, int dim) {
+  EventSpan e = event_span(p, b);
+  if (rows_interleaved(p) && p.qkv_row_stride) {
+    e.rs1 = p.qkv_row_stride / dim;
+    e.base1 = e.row0 * e.rs1;
+  }
+  return e;
+}
+
 // Element offset of (row i of the event, head h, 0) in a [*, H, dim] (packed)
 // or [B, H, L, dim] (padded) tensor.
 __device__ __forceinline__ int64_t ev_off(const EventSpan& e, int i, int h, int dim) {
@@ -109,6 +121,17 @@ __device__ __forceinline__ int64_t vec_off(const FstProblem& p, int64_t row, int
 // packed [T, H, D] rows are H*D apart, padded [B, H, L, D] rows D apart.
 __device__ __forceinline__ int row_stride(const FstProblem& p, int dim) {
   return rows_interleaved(p) ? p.heads * dim : dim;
+}
+
+// row_stride for q, k, v, dq, dk, dv (the caller's qkv_row_stride if set).
+__device__ __forceinline__ int qkv_row_stride(const FstProblem& p, int dim) {
+  return (rows_interleaved(p) && p.qkv_row_stride) ? p.qkv_row_stride : row_stride(p, dim);
+}
+
+// vec_off for q, k, v, dq, dk, dv.
+__device__ __forceinline__ int64_t qkv_off(const FstProblem& p, int64_t row, int h, int dim) {
+  if (rows_interleaved(p) && p.qkv_row_stride) return row * p.qkv_row_stride + (int64_t)h * dim;
+  return vec_off(p, row, h, dim);
 }
 
 // Offset of (row, head) in a per-row-per-head fp32 vector (LSE, D, sigma).

@@ -88,6 +88,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
   const T* u = (const T*)a.u;
   T* out = (T*)a.out;
   const int64_t off = vec_off(p, t.row, t.h, D);
+  const int64_t qoff = qkv_off(p, t.row, t.h, D);
   if (t.i >= t.ev.len) {  // padding row (padded layout only)
     for (int d = 0; d < D; ++d) out[off + d] = from_f<T>(0.f);
     a.lse[stat_off(p, t.row, t.h)] = 0.f;
@@ -97,14 +98,14 @@ __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
   float qt[kMax], uu[kMax], acc[kMax], ae[kMax], e[kMax];
 #pragma unroll
   for (int d = 0; d < kMax; ++d) {
-    qt[d] = d < D ? to_f<T>(q[off + d]) * p.scale : 0.f;
+    qt[d] = d < D ? to_f<T>(q[qoff + d]) * p.scale : 0.f;
     acc[d] = 0.f;
   }
   const int64_t uoff = vec_off(p, t.row, t.h, C);
 #pragma unroll
   for (int c = 0; c < kMax; ++c) {
     uu[c] = (p.use_attn_bias && c < C)
-                ? (u ? to_f<T>(u[uoff + c]) : project<T>(p, q, off, p.scale, c, D, C))
+                ? (u ? to_f<T>(u[uoff + c]) : project<T>(p, q, qoff, p.scale, c, D, C))
                 : 0.f;
     ae[c] = 0.f;
     e[c] = 0.f;
@@ -113,7 +114,7 @@ __global__ void __launch_bounds__(128) fwd_kernel(FstForwardArgs a) {
   float m = -INFINITY, l = 0.f;
   for (int j = 0; j < t.ev.len; ++j) {
     const int64_t krow = t.ev.row0 + j;
-    const int64_t koff = vec_off(p, krow, t.h, D);
+    const int64_t koff = qkv_off(p, krow, t.h, D);
     float s = 0.f;
 #pragma unroll
     for (int d = 0; d < kMax; ++d)
@@ -174,13 +175,14 @@ __device__ __forceinline__ void load_bwd_row(const FstBackwardArgs& a, int64_t r
   const FstProblem& p = a.prob;
   const int D = p.head_dim, C = p.channels;
   const int64_t off = vec_off(p, row, h, D), coff = vec_off(p, row, h, C);
+  const int64_t qoff = qkv_off(p, row, h, D);
   const T* q = (const T*)a.q;
   const T* dout = (const T*)a.dout;
   const T* o = (const T*)a.out;
   float c = 0.f;
 #pragma unroll
   for (int d = 0; d < kMax; ++d) {
-    r.qt[d] = d < D ? to_f<T>(q[off + d]) * p.scale : 0.f;
+    r.qt[d] = d < D ? to_f<T>(q[qoff + d]) * p.scale : 0.f;
     r.dov[d] = d < D ? to_f<T>(dout[off + d]) : 0.f;
     if (d < D && o) {
       float od = to_f<T>(o[off + d]);
@@ -193,7 +195,7 @@ __device__ __forceinline__ void load_bwd_row(const FstBackwardArgs& a, int64_t r
     r.uu[c] = 0.f;
     r.wt[c] = 0.f;
     if (c < C && p.use_attn_bias)
-      r.uu[c] = a.u ? to_f<T>(((const T*)a.u)[coff + c]) : project<T>(p, q, off, p.scale, c, D, C);
+      r.uu[c] = a.u ? to_f<T>(((const T*)a.u)[coff + c]) : project<T>(p, q, qoff, p.scale, c, D, C);
     if (c < C && p.use_act_bias)
       r.wt[c] = a.wt ? to_f<T>(((const T*)a.wt)[coff + c]) : project<T>(p, dout, off, 1.f, c, D, C);
   }
@@ -247,7 +249,7 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
   RowTask t;
   if (!row_task(p, (int64_t)blockIdx.x * blockDim.x + threadIdx.x, t)) return;
   const int D = p.head_dim, C = p.channels;
-  const int64_t off = vec_off(p, t.row, t.h, D), coff = vec_off(p, t.row, t.h, C);
+  const int64_t off = qkv_off(p, t.row, t.h, D), coff = vec_off(p, t.row, t.h, C);
   const int64_t so = stat_off(p, t.row, t.h);
   T* dq = (T*)a.dq;
   if (t.i >= t.ev.len) {
@@ -276,7 +278,7 @@ __global__ void __launch_bounds__(128) bwd_rows_kernel(FstBackwardArgs a, float*
   float acc_a = 0.f, acc_p = 0.f;
   for (int j = 0; j < t.ev.len; ++j) {
     const int64_t krow = t.ev.row0 + j;
-    const int64_t koff = vec_off(p, krow, t.h, D);
+    const int64_t koff = qkv_off(p, krow, t.h, D);
     load_vec<T>(k, koff, D, kv);
     load_vec<T>(v, koff, D, vv);
     float P, dP;
@@ -337,7 +339,7 @@ __global__ void __launch_bounds__(128) bwd_cols_kernel(FstBackwardArgs a) {
   RowTask t;
   if (!row_task(p, (int64_t)blockIdx.x * blockDim.x + threadIdx.x, t)) return;
   const int D = p.head_dim;
-  const int64_t off = vec_off(p, t.row, t.h, D);
+  const int64_t off = qkv_off(p, t.row, t.h, D);
   T* dk = (T*)a.dk;
   T* dv = (T*)a.dv;
   if (t.i >= t.ev.len) {
@@ -395,7 +397,8 @@ __global__ void __launch_bounds__(256) dw_partial_kernel(FstBackwardArgs a, cons
         if (row - b * p.max_len >= p.seqlens[b]) continue;
       }
       const int64_t off = vec_off(p, row, h, D), coff = vec_off(p, row, h, C);
-      if (p.use_attn_bias) acc = fmaf(to_f<T>(q[off + d]) * p.scale, hbuf[coff + c], acc);
+      if (p.use_attn_bias)
+        acc = fmaf(to_f<T>(q[qkv_off(p, row, h, D) + d]) * p.scale, hbuf[coff + c], acc);
       if (p.use_act_bias) acc = fmaf(to_f<T>(dout[off + d]), gbuf[coff + c], acc);
     }
     a.dw_partial[(int64_t)blockIdx.x * D * C + o] = acc;

@@ -110,6 +110,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     b = p.event_order ? p.event_order[lo] : lo;
   }
   const EventSpan ev = event_span(p, b);
+  const EventSpan evq = qkv_span(p, b, DH);  // k, v, dk, dv (a fused QKV buffer's row stride)
   const int k0 = kb * S::BK;
   const int h0 = blockIdx.z * heads_per_group;
   const int NH = min(heads_per_group, p.heads - h0);
@@ -130,7 +131,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
         const int c = idx % CH, r = idx / CH;
         const int h = h0 + r / S::BK, j = k0 + r % S::BK;
         if (j >= p.max_len) continue;
-        const int64_t off = ev_off(ev, j, h, DH) + c * 8;
+        const int64_t off = ev_off(evq, j, h, DH) + c * 8;
         *(uint4*)(gdk + off) = make_uint4(0, 0, 0, 0);
         *(uint4*)(gdv + off) = make_uint4(0, 0, 0, 0);
       }
@@ -151,7 +152,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
       const int c = idx % CH, j = (idx / CH) % S::BK, h = idx / (CH * S::BK);
       const uint32_t off = h * S::BK * S::RBD + swz<S::RBD>(j, c);
       if (j < nvalid_k) {
-        const int64_t go = ev_off(ev, k0 + j, h0 + h, DH) + c * 8;
+        const int64_t go = ev_off(evq, k0 + j, h0 + h, DH) + c * 8;
         cp_async16(sm + S::OFF_KS + off, gk + go);
         cp_async16(sm + S::OFF_VS + off, gv + go);
       } else {
@@ -580,7 +581,7 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
     const int j = r8 + 8 * rh;
     const bool valid = j < nvalid_k;
     if (!valid && (is_varlen(p) || k0 + j >= p.max_len)) continue;
-    const int64_t off = ev_off(ev, k0 + j, h, DH);
+    const int64_t off = ev_off(evq, k0 + j, h, DH);
 #pragma unroll
     for (int nd = 0; nd < S::NTD; ++nd) {
       const int d = nd * 8 + 2 * m4;

@@ -156,6 +156,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   float* dwp = a.dw_partial + part * DH * C;
   float* dbp = a.db_partial + part * DH;
   const EventSpan ev = event_span(p, b);
+  const EventSpan evq = qkv_span(p, b, DH);  // q, k, v, dq (a fused QKV buffer's row stride)
   const int q0 = qb * S::BM;
   const int h0 = blockIdx.z * heads_per_group;
   const int NH = min(heads_per_group, p.heads - h0);
@@ -179,7 +180,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         const int c = idx % CH, r = idx / CH;
         const int h = h0 + r / S::BM, q = q0 + r % S::BM;
         if (q >= p.max_len) continue;
-        *(uint4*)(gdq + ev_off(ev, q, h, DH) + c * 8) = make_uint4(0, 0, 0, 0);
+        *(uint4*)(gdq + ev_off(evq, q, h, DH) + c * 8) = make_uint4(0, 0, 0, 0);
         if (c == 0) {
           const int64_t so = ev_off(ev, q, h, 1);
           a.delta[so] = 0.f;
@@ -211,7 +212,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
       if (q < nvalid_q) {
         const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
-        cp_async16(sm + S::OFF_QR + off, gq + go);
+        cp_async16(sm + S::OFF_QR + off, gq + ev_off(evq, q0 + q, h0 + h, DH) + c * 8);
         cp_async16(sm + S::OFF_DOR + off, gdo + go);
         if (gout) cp_async16(sm + S::OFF_OS + off, gout + go);
       } else {
@@ -346,7 +347,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
         if (q < nvalid_q) {  // raw q (scaled in place after the projections)
           const int64_t go = ev_off(ev, q0 + q, h0 + h, DH) + c * 8;
-          vq = *(const uint4*)(gq + go);
+          vq = *(const uint4*)(gq + ev_off(evq, q0 + q, h0 + h, DH) + c * 8);
           vd = *(const uint4*)(gdo + go);
         }
         const uint32_t off = h * S::BM * S::RBD + swz<S::RBD>(q, c);
@@ -721,9 +722,9 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     const uint32_t v_ring = sm + S::OFF_V + hl * S::BN * S::RBD;
     // K / V of this head: event base pointer and row stride (no 64-bit math
     // per copy).
-    const T* __restrict__ kbase = gk + ev_off(ev, 0, h, DH);
-    const T* __restrict__ vbase = gv + ev_off(ev, 0, h, DH);
-    const int rs = row_stride(p, DH);
+    const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
+    const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
+    const int rs = qkv_row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
         constexpr int CH = DH / 8;
@@ -913,7 +914,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       const int q = r8 + 8 * rh;
       const bool valid = q < nvalid_q;
       if (!valid && (is_varlen(p) || q0 + q >= p.max_len)) continue;
-      T* orow = gdq + ev_off(ev, q0 + q, h, DH);
+      T* orow = gdq + ev_off(evq, q0 + q, h, DH);
 #pragma unroll
       for (int nd = 0; nd < S::NTD; ++nd) {
         const int d = nd * 8 + 2 * m4;
@@ -951,7 +952,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       uint4 vq = make_uint4(0, 0, 0, 0), vd = make_uint4(0, 0, 0, 0);
       if (q < nvalid_q) {
         const int64_t go = ev_off(ev, q0 + q, h0 + hl, DH) + c * 8;
-        vq = *(const uint4*)(gq + go);
+        vq = *(const uint4*)(gq + ev_off(evq, q0 + q, h0 + hl, DH) + c * 8);
         vd = *(const uint4*)(gdo + go);
       }
       const uint32_t so = hl * S::BM * S::RBD + swz<S::RBD>(q, c);

@@ -161,6 +161,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   int b, qb;
   if (!fwd_tile(p, tile_start, b, qb)) return;
   const EventSpan ev = event_span(p, b);
+  const EventSpan evq = qkv_span(p, b, DH);  // q, k, v (a fused QKV buffer's row stride)
   const int q0 = qb * S::BM;
   // Heads are split into gridDim.z groups of heads_per_group (<= HP); the
   // block is sized for heads_per_group head warps, so in a shorter last group
@@ -215,7 +216,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       const int c = idx % QCH, q = (idx / QCH) % S::BM, h = idx / (QCH * S::BM);
       const uint32_t off = S::OFF_Q + h * S::BM * S::RBD + swz<S::RBD>(q, c);
       if (q < nvalid_q)
-        cp_async16(sm + off, gq + ev_off(ev, q0 + q, h0 + h, DH) + c * 8);
+        cp_async16(sm + off, gq + ev_off(evq, q0 + q, h0 + h, DH) + c * 8);
       else
         *(uint4*)(smem + off) = make_uint4(0, 0, 0, 0);
     }
@@ -547,9 +548,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     // Private ring of this head's K and V chunks: [2 stages][BN][DHP].
     // K / V of this head: event base pointer and row stride (no 64-bit math
     // per copy).
-    const T* __restrict__ kbase = gk + ev_off(ev, 0, h, DH);
-    const T* __restrict__ vbase = gv + ev_off(ev, 0, h, DH);
-    const int rs = row_stride(p, DH);
+    const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
+    const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
+    const int rs = qkv_row_stride(p, DH);
     auto load_kv = [&](int n) {
       if (n < nchunks) {
         constexpr int CH = DH / 8;

@@ -54,7 +54,8 @@ __all__ = [
 def __getattr__(name: str) -> object:
     """Resolve the fused entry points lazily (they need the CUDA library)."""
     if name in ("flash_spacetime_attention", "flash_spacetime_attention_varlen",
-                "flash_spacetime_attention_nested", "flash_spacetime_forward",
+                "flash_spacetime_attention_nested", "flash_spacetime_attention_qkv",
+                "flash_spacetime_forward",
                 "flash_spacetime_backward", "upload_valid_rows"):
         from . import ops
 

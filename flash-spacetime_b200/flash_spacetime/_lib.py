@@ -21,7 +21,7 @@ FST_ERR_CUDA = 3
 FST_ERR_WORKSPACE = 4
 FST_ERR_DEVICE = 5
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 
 EXPORTED = (
     "fst_abi_version",
@@ -58,6 +58,7 @@ class FstProblem(ctypes.Structure):
         ("weight", ctypes.c_void_p),
         ("bias", ctypes.c_void_p),
         ("event_order", ctypes.c_void_p),
+        ("qkv_row_stride", ctypes.c_int32),
     ]
 
 

@@ -133,9 +133,11 @@ class _Problem:
         use_act_bias: bool,
         layout: str = "bhld",
         host_projection: bool = False,
+        qkv_row_stride: int = 0,
     ) -> None:
         self.packed = cu_seqlens is not None
         self.host_projection = bool(host_projection)
+        self.qkv_row_stride = int(qkv_row_stride)
         if layout not in ("bhld", "blhd"):
             raise ValueError(f"layout must be 'bhld' or 'blhd', got {layout!r}")
         self.layout = "packed" if self.packed else layout
@@ -229,6 +231,7 @@ class _Problem:
         p.weight = _ptr(self.w32)
         p.bias = _ptr(self.b32)
         p.event_order = _ptr(self.order)
+        p.qkv_row_stride = self.qkv_row_stride
         return p
 
     def stat_shape(self) -> Tuple[int, ...]:
@@ -269,7 +272,7 @@ def fused_forward(pb: _Problem, q: Tensor, k: Tensor, v: Tensor) -> Tuple[Tensor
     # round trips. With host_projection the host forms it as upstream does
     # and passes it through the C ABI.
     u = _host_u(pb, q)
-    out = torch.empty_like(q)
+    out = torch.empty(q.shape, dtype=q.dtype, device=q.device)
     lse = torch.empty(pb.stat_shape(), dtype=torch.float32, device=pb.device)
     a = _lib.FstForwardArgs()
     a.prob = pb.c_struct()
@@ -292,19 +295,25 @@ def fused_backward(
     lse: Tensor,
     dout: Tensor,
     want_absmax: bool = False,
+    dqkv: Optional[Tensor] = None,
 ) -> Dict[str, Optional[Tensor]]:
     """One ``fst_backward`` call plus the two deterministic host reductions.
 
     Returns dq, dk, dv (input dtype), dW ``[Dh, C]`` and db ``[Dh]`` (fp32,
     or None when the projection is unused), and the per-row diagnostics
-    delta (D), sigma (rowsum dS) and, on request, rowmax |dS|.
+    delta (D), sigma (rowsum dS) and, on request, rowmax |dS|. With a fused
+    QKV problem the gradients are written into ``dqkv`` (``[rows, 3, H,
+    Dh]``) and dq, dk, dv are its views.
     """
     lib = _lib.load()
     dout, out, lse = _dense(dout), _dense(out), lse.contiguous()
     # u and w~ = dO @ W (upstream backward.py:541-556) are formed in-kernel,
     # or on the host with host_projection.
     u, wt = _host_u(pb, q), _host_wt(pb, dout)
-    dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
+    if dqkv is not None:
+        dq, dk, dv = dqkv.select(-3, 0), dqkv.select(-3, 1), dqkv.select(-3, 2)
+    else:
+        dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
     a = _lib.FstBackwardArgs()
     a.prob = pb.c_struct()
     nparts = int(lib.fst_dw_partial_count(ctypes.byref(a.prob)))
@@ -472,6 +481,100 @@ def flash_spacetime_attention_varlen(
         q, k, v, feats, weight, bias, None, cu_seqlens,
         scale, use_attn_bias, use_activation_bias, "bhld", host_projection,
     )
+
+
+class _FlashSpacetimeQKV(torch.autograd.Function):
+    """The fused op on one QKV buffer ``[rows, 3, H, Dh]``, read in place
+    through the C ABI's ``qkv_row_stride``; the backward writes the gradient
+    of the same buffer in one piece."""
+
+    @staticmethod
+    def forward(  # type: ignore[override]
+        ctx: Any,
+        qkv: Tensor,
+        feats: Tensor,
+        weight: Tensor,
+        bias: Optional[Tensor],
+        seqlens: Optional[Tensor],
+        cu_seqlens: Optional[Tensor],
+        scale: Optional[float],
+        use_attn_bias: bool,
+        use_activation_bias: bool,
+        host_projection: bool,
+    ) -> Tensor:
+        if feats.requires_grad:
+            raise ValueError("feats (detector data) must not require grad")
+        qkv = _dense(qkv)
+        q, k, v = qkv.select(-3, 0), qkv.select(-3, 1), qkv.select(-3, 2)
+        heads, dim = q.shape[-2], q.shape[-1]
+        pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale, use_attn_bias,
+                      use_activation_bias, "blhd", host_projection, 3 * heads * dim)
+        out, lse = fused_forward(pb, q, k, v)
+        ctx.save_for_backward(qkv, out, lse)
+        ctx.pb = pb
+        ctx.weight_dtype = weight.dtype
+        ctx.bias_dtype = None if bias is None else bias.dtype
+        return out
+
+    @staticmethod
+    def backward(ctx: Any, grad_out: Tensor) -> Tuple[Optional[Tensor], ...]:  # type: ignore[override]
+        qkv, out, lse = ctx.saved_tensors
+        pb: _Problem = ctx.pb
+        q, k, v = qkv.select(-3, 0), qkv.select(-3, 1), qkv.select(-3, 2)
+        dqkv = torch.empty_like(qkv)
+        g = fused_backward(pb, q, k, v, out, lse, grad_out, dqkv=dqkv)
+        proj_used = pb.attn or pb.act
+        need = ctx.needs_input_grad
+        dw = g["dW"].to(ctx.weight_dtype) if (proj_used and need[2]) else None
+        db = None
+        if ctx.bias_dtype is not None and proj_used and need[3]:
+            db = g["db"].to(ctx.bias_dtype)
+        return (dqkv if need[0] else None, None, dw, db, None, None, None, None, None, None)
+
+
+def flash_spacetime_attention_qkv(
+    qkv: Tensor,
+    feats: Tensor,
+    weight: Tensor,
+    bias: Optional[Tensor],
+    seqlens: Optional[Tensor] = None,
+    scale: Optional[float] = None,
+    use_attn_bias: bool = True,
+    use_activation_bias: bool = True,
+    *,
+    cu_seqlens: Optional[Tensor] = None,
+    key_padding_mask: Optional[Tensor] = None,
+    validate_mask: bool = True,
+    host_projection: bool = False,
+) -> Tensor:
+    """The op on a fused QKV projection, read in place (no head split).
+
+    ``qkv``: ``[B, L, 3, H, Dh]`` (padded, with ``seqlens`` or a mask as for
+    :func:`flash_spacetime_attention`) or ``[T, 3, H, Dh]`` (packed, with
+    ``cu_seqlens``) -- the output of one ``nn.Linear(model_dim, 3 * H * Dh)``
+    viewed per head. Upstream builds q, k and v with three projections and a
+    head split (reference.py:187-223, ``split_heads``); here the kernels read
+    each row's q, k and v where the projection wrote them, and the gradient
+    comes back as one ``[.., 3, H, Dh]`` tensor. Returns ``[B, L, H, Dh]``
+    (or ``[T, H, Dh]``) in qkv's dtype with padding rows exactly 0.
+    """
+    if qkv.dim() not in (4, 5) or qkv.shape[-3] != 3:
+        raise ValueError(f"qkv must be [B, L, 3, H, Dh] or [T, 3, H, Dh], got {tuple(qkv.shape)}")
+    packed = cu_seqlens is not None
+    if packed != (qkv.dim() == 4):
+        raise ValueError("a [T, 3, H, Dh] qkv needs cu_seqlens; a [B, L, 3, H, Dh] one does not")
+    if not packed:
+        if key_padding_mask is not None:
+            if seqlens is not None:
+                raise ValueError("pass seqlens or key_padding_mask, not both")
+            seqlens = seqlens_from_mask(key_padding_mask, validate_mask)
+        elif seqlens is None:
+            seqlens = torch.full((qkv.shape[0],), qkv.shape[1], dtype=torch.int32,
+                                 device=qkv.device)
+        elif seqlens.dim() == 2:
+            seqlens = seqlens_from_mask(seqlens, validate_mask)
+    return _FlashSpacetimeQKV.apply(qkv, feats, weight, bias, seqlens, cu_seqlens, scale,
+                                    use_attn_bias, use_activation_bias, host_projection)
 
 
 def flash_spacetime_attention_nested(

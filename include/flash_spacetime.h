@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FST_ABI_VERSION 3
+#define FST_ABI_VERSION 4
 
 /* Storage dtype of q, k, v, u, wt, out, dout, dq, dk, dv. */
 enum FstDtype { FST_F32 = 0, FST_BF16 = 1, FST_F16 = 2 };
@@ -96,6 +96,15 @@ typedef struct FstProblem {
    * NULL = natural order. Results do not depend on it. No upstream
    * counterpart. */
   const int32_t* event_order;
+  /* Elements between consecutive rows of q, k, v and of dq, dk, dv in the
+   * row-interleaved layouts (packed == 1 or 2); 0 = H*Dh (dense rows). A fused
+   * QKV projection [rows, 3, H, Dh] -- one [rows, 3*H*Dh] buffer -- is read
+   * in place with q = base, k = base + H*Dh, v = base + 2*H*Dh and
+   * qkv_row_stride = 3*H*Dh, and the gradients written into a buffer of the
+   * same form (upstream builds q, k, v by three projections and a head split,
+   * reference.py:187-223). Must be a multiple of Dh and of 8 elements, and
+   * >= H*Dh; 0 for the padded [B,H,L,D] layout. out, dout, u, wt stay dense. */
+  int32_t qkv_row_stride;
 } FstProblem;
 
 typedef struct FstForwardArgs {

@@ -289,3 +289,50 @@ def test_empty_and_equal_length_events(dtype):
                             case["bias"], case["cu"].tolist())
     err = cs.normwise(out_v.double().cpu(), ref["out"])
     assert err <= cs.NORMWISE[dtype] if dtype != torch.float32 else err <= 1e-3
+
+
+@pytest.mark.parametrize("packed", [False, True])
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16, torch.float32])
+def test_fused_qkv_matches_separate(packed, dtype):
+    # One [rows, 3, H, Dh] QKV buffer (a fused projection) read in place through
+    # qkv_row_stride: output, the fused gradient and dW/db equal the separate
+    # q/k/v path bit for bit.
+    from flash_spacetime.ops import flash_spacetime_attention_qkv
+
+    case = cs.padded_case(3, 70, 12, 32, 16, True, seed=808)
+    lens = [int(n) for n in case["seqlens"]]
+    pk = cs.packed_from_padded(case)
+    if packed:
+        q, k, v, go = (_to(pk[x], dtype) for x in ("q", "k", "v", "grad"))  # [T, H, D]
+        feats = pk["feats"].cuda()
+    else:
+        q, k, v, go = (_to(case[x], dtype).transpose(1, 2).contiguous()
+                       for x in ("q", "k", "v", "grad"))  # [B, L, H, D]
+        feats = case["feats"].cuda()
+    res = []
+    for fused in (False, True):
+        w = _to(case["weight"], torch.float32).requires_grad_(True)
+        b = _to(case["bias"], torch.float32).requires_grad_(True)
+        if fused:
+            qkv = torch.stack((q, k, v), dim=-3).requires_grad_(True)  # [.., 3, H, D]
+            if packed:
+                out = flash_spacetime_attention_qkv(qkv, feats, w, b, cu_seqlens=pk["cu"].cuda())
+            else:
+                out = flash_spacetime_attention_qkv(qkv, feats, w, b, case["seqlens"].cuda())
+            out.backward(go)
+            grads = qkv.grad.unbind(-3)
+        else:
+            leaves = [t.clone().requires_grad_(True) for t in (q, k, v)]
+            if packed:
+                out = flash_spacetime_attention_varlen(*leaves, feats, w, b, pk["cu"].cuda())
+            else:
+                out = flash_spacetime_attention(*leaves, feats, w, b, case["seqlens"].cuda(),
+                                                layout="blhd")
+            out.backward(go)
+            grads = [t.grad for t in leaves]
+        res.append((out.detach(), *grads, w.grad.clone(), b.grad.clone()))
+    for a, b_ in zip(res[0], res[1]):
+        assert torch.equal(a, b_)
+    if not packed:
+        for i, n in enumerate(lens):  # padding rows of out and of the fused gradient are 0
+            assert torch.count_nonzero(res[1][0][i, n:]) == 0

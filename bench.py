@@ -101,14 +101,14 @@ def _dist_setup():
     return world, rank, local
 
 
-def _workload_lengths(name: str, world: int, rank: int, seed: int):
+def _workload_lengths(name: str, world: int, rank: int, seed: int, events: int = 0):
     """(lengths of this rank's shard, padded length or None, global event
     count, every rank's shard lengths)."""
     from flash_spacetime.sharding import lpt_partition
     from flash_spacetime.synthetic import lengths_for
 
     if name == "config1":
-        lens, padlen = lengths_for("config1", 256 * world, seed), 768
+        lens, padlen = lengths_for("config1", (events or 256) * world, seed), 768
     elif name == "config2":
         lens, padlen = [1024] * (128 * world), 1024
     elif name == "config3":
@@ -344,7 +344,8 @@ def run_ours(args):
     from flash_spacetime import _lib, ops, synthetic
     from flash_spacetime.sharding import RowGather, max_over_ranks, ordered_sum
 
-    lens, padlen, n_events, per_rank = _workload_lengths(args.workload, world, rank, args.seed)
+    lens, padlen, n_events, per_rank = _workload_lengths(args.workload, world, rank, args.seed,
+                                                         args.events)
     heads, dim, channels, dtype_name, metric = _shape(args)
     dtype = {"bf16": torch.bfloat16, "fp16": torch.float16}[dtype_name]
     scaled = args.coords == "scaled"
@@ -525,6 +526,8 @@ def main():
     ap.add_argument("--dim", type=int, default=0, help="config2 head dim (32 or 64)")
     ap.add_argument("--channels", type=int, default=0, help="config2 channels (32 or 64)")
     ap.add_argument("--dtype", default="bf16", choices=("bf16", "fp16"), help="config2 dtype")
+    ap.add_argument("--events", type=int, default=0,
+                    help="config1 events per GPU (default 256; smaller for profiler captures)")
     ap.add_argument("--no-gather", action="store_true",
                     help="multi-GPU: skip the all-gather of the outputs")
     ap.add_argument("--coords", default="raw", choices=("raw", "scaled"))

@@ -66,11 +66,26 @@ def _run(data, packed):
 FLOOR = 1e-2
 
 
+# Worst normwise error seen per quantity in the running test (printed with -s).
+WORST = {}
+
+
 def _check(what, kernel, ref):
     kernel, ref = kernel.cpu().double(), ref.double()
     den = max(ref.norm().item(), FLOOR * ref.numel() ** 0.5)
     err = (kernel - ref).norm().item() / den
+    key = what.split()[-1]
+    WORST[key] = max(WORST.get(key, 0.0), err)
     assert err <= TOL, f"{what}: normwise error {err:.3e} > {TOL}"
+
+
+@pytest.fixture(autouse=True)
+def _report_worst(request):
+    WORST.clear()
+    yield
+    if WORST:
+        worst = ", ".join(f"{k} {v:.2e}" for k, v in sorted(WORST.items()))
+        print(f"\n{request.node.name}: worst normwise error: {worst}")
 
 
 def _subset(data, events, packed):
@@ -174,6 +189,7 @@ def test_config1_full_batch():
     res = _run(data, packed=False)
     valid = (torch.arange(768, device="cuda")[None, :] < data["seqlens"][:, None])[:, None, :]
     ratio = _rowsum_ratio(res, valid.expand_as(res["sigma"]))
+    WORST["rowsum(dS)/rowmax|dS|"] = ratio
     assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
     order = sorted(range(len(lens)), key=lambda i: (-lens[i], i))
     gen = torch.Generator().manual_seed(SEED)
@@ -190,6 +206,7 @@ def test_config2_wide_channels(dim, channels, dtype):
                                   SEED + dim + channels)
     res = _run(data, packed=False)
     ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    WORST["rowsum(dS)/rowmax|dS|"] = ratio
     assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
     _check_events(data, res, [127], packed=False)
 
@@ -199,6 +216,7 @@ def test_config3_packed_events():
     data = synthetic.packed_batch(lens, 12, 32, 16, torch.bfloat16, torch.device("cuda"), SEED)
     res = _run(data, packed=True)
     ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    WORST["rowsum(dS)/rowmax|dS|"] = ratio
     assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
     gen = torch.Generator().manual_seed(SEED)
     singles = [i for i, n in enumerate(lens) if n == 1]
@@ -215,5 +233,6 @@ def test_config4_uncapped_event():
     data = synthetic.packed_batch(lens, 12, 32, 16, torch.bfloat16, torch.device("cuda"), SEED)
     res = _run(data, packed=True)
     ratio = _rowsum_ratio(res, torch.ones_like(res["sigma"], dtype=torch.bool))
+    WORST["rowsum(dS)/rowmax|dS|"] = ratio
     assert ratio < 1e-6, f"max |rowsum dS| / rowmax |dS| = {ratio:.3e}"
     _check_long_event(data, res, 0, 128, SEED)

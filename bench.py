@@ -309,7 +309,8 @@ def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, e
             buf = slots[slot]
             lv = {k: buf[k].detach().requires_grad_(True)
                   for k in ("q", "k", "v", "weight", "bias")}
-            _, dw, db = step(lv, buf["feats"], buf["grad"], buf["index"])
+            # The next step's upload runs beside this step on every SM.
+            _, dw, db = step(lv, buf["feats"], buf["grad"], buf["index"], share_sms=True)
             dw_host.copy_(torch.cat([dw.flatten().float(), db.flatten().float()]),
                           non_blocking=True)
             free[slot].record()
@@ -329,7 +330,7 @@ def run_e2e(args, data, index, step, device, world, total_flops, lens, padded, e
         raise RuntimeError("e2e: dW/db differ from the device-resident run")
     return {"value": total_flops / (e2e_ms * 1e-3) / 1e12, "unit": "TFLOP/s",
             "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-            "overlap": "next step's host->device copy on a side stream",
+            "overlap": "next step's host->device copy on a side stream (share_sms hint)",
             "transfer": ("valid rows only (upload_valid_rows: gather kernel reading pinned "
                          "host memory)" if padded else "whole tensors")}
 
@@ -378,15 +379,16 @@ def run_ours(args):
             idx = None
         gather = RowGather(sizes, (dim,), dtype, device)
 
-    def step(lv, feats_, grad_, seq_or_cu):
+    def step(lv, feats_, grad_, seq_or_cu, share_sms=False):
         for t in lv.values():
             t.grad = None
         if padlen is not None:
             out = ops.flash_spacetime_attention(lv["q"], lv["k"], lv["v"], feats_, lv["weight"],
-                                                lv["bias"], seq_or_cu)
+                                                lv["bias"], seq_or_cu, share_sms=share_sms)
         else:
             out = ops.flash_spacetime_attention_varlen(lv["q"], lv["k"], lv["v"], feats_,
-                                                       lv["weight"], lv["bias"], seq_or_cu)
+                                                       lv["weight"], lv["bias"], seq_or_cu,
+                                                       share_sms=share_sms)
         work = None
         if gather is not None:
             rows = out.detach().view(-1, dim)

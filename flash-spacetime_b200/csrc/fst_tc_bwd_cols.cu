@@ -85,10 +85,11 @@ __device__ __forceinline__ int cb_bias_full(int s) { return 1 + s; }
 __device__ __forceinline__ int cb_bias_empty(int s) { return 3 + s; }
 
 template <typename T, int DH, int C>
-__global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
-    bwd_cols_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
-                       int heads_per_group, const T* __restrict__ gu,
-                       const T* __restrict__ gwt, const T* __restrict__ gqt) {
+__device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
+                                              const int* __restrict__ tile_start,
+                                              int heads_per_group, const T* __restrict__ gu,
+                                              const T* __restrict__ gwt,
+                                              const T* __restrict__ gqt) {
   using S = ColShape<DH, C>;
   using E = Elem<T>;
   extern __shared__ __align__(128) unsigned char smem[];
@@ -596,6 +597,34 @@ __global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
 // ---------------------------------------------------------------------------
 
 template <typename T, int DH, int C>
+__global__ void __launch_bounds__(ColShape<DH, C>::NWARPS * 32, 1)
+    bwd_cols_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
+                       int heads_per_group, const T* __restrict__ gu,
+                       const T* __restrict__ gwt, const T* __restrict__ gqt) {
+  bwd_cols_body<T, DH, C>(a, tile_start, heads_per_group, gu, gwt, gqt);
+}
+
+// The same kernel held to 120 registers a thread (a few bytes of spills):
+// 512 x 120 registers leave 4096 of an SM's 65536 free, room for a small
+// kernel running beside it on every SM -- the host-to-device row gather of a
+// training loop's next batch (fst_upload_rows, 128 threads x <= 32 registers),
+// which cannot start on an SM that this kernel fills. Chosen when the caller
+// sets FST_FLAG_SHARE_SMS; costs about 7 % of the backward when nothing runs
+// beside it. Only the narrow shapes have the variant.
+template <typename T, int DH, int C>
+__global__ void __maxnreg__(120)
+    bwd_cols_tc_shared_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
+                              int heads_per_group, const T* __restrict__ gu,
+                              const T* __restrict__ gwt, const T* __restrict__ gqt) {
+  bwd_cols_body<T, DH, C>(a, tile_start, heads_per_group, gu, gwt, gqt);
+}
+
+template <int DH, int C>
+constexpr bool has_shared_variant() {
+  return DH <= 32 && C <= 16 && ColShape<DH, C>::NWARPS * 32 * 120 <= 65536 - 4096;
+}
+
+template <typename T, int DH, int C>
 static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* tile_start,
                              const void* gu, const void* gwt, const void* gqt) {
   using S = ColShape<DH, C>;
@@ -603,8 +632,11 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   if constexpr (!S::kFits) {
     return FST_ERR_UNSUPPORTED;
   } else {
-    static std::atomic<uint64_t> configured{0};
-    if (allow_dynamic_smem((const void*)bwd_cols_tc_kernel<T, DH, C>, S::SMEM, configured))
+    const bool shared = has_shared_variant<DH, C>() && (p.flags & FST_FLAG_SHARE_SMS);
+    const void* fn = shared ? (const void*)bwd_cols_tc_shared_kernel<T, DH, C>
+                            : (const void*)bwd_cols_tc_kernel<T, DH, C>;
+    static std::atomic<uint64_t> configured{0}, configured_shared{0};
+    if (allow_dynamic_smem(fn, S::SMEM, shared ? configured_shared : configured))
       return FST_ERR_CUDA;
     const int groups = (p.heads + S::HP - 1) / S::HP;
     const int per_group = (p.heads + groups - 1) / groups;
@@ -618,8 +650,12 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
       grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
     }
     if (grid.x == 0 || grid.y == 0) return FST_OK;
-    bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
-                                                                 (const T*)gu, (const T*)gwt, (const T*)gqt);
+    if (shared)
+      bwd_cols_tc_shared_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
+          a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
+    else
+      bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
+          a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
     count_launch();
     return FST_OK;
   }

@@ -22,6 +22,7 @@ FST_ERR_WORKSPACE = 4
 FST_ERR_DEVICE = 5
 
 ABI_VERSION = 4
+FST_FLAG_SHARE_SMS = 1  # FstProblem.flags: another kernel shares the SMs
 
 EXPORTED = (
     "fst_abi_version",
@@ -59,6 +60,7 @@ class FstProblem(ctypes.Structure):
         ("bias", ctypes.c_void_p),
         ("event_order", ctypes.c_void_p),
         ("qkv_row_stride", ctypes.c_int32),
+        ("flags", ctypes.c_int32),
     ]
 
 

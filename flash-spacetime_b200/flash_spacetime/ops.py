@@ -134,8 +134,10 @@ class _Problem:
         layout: str = "bhld",
         host_projection: bool = False,
         qkv_row_stride: int = 0,
+        share_sms: bool = False,
     ) -> None:
         self.packed = cu_seqlens is not None
+        self.share_sms = bool(share_sms)
         self.host_projection = bool(host_projection)
         self.qkv_row_stride = int(qkv_row_stride)
         if layout not in ("bhld", "blhd"):
@@ -232,6 +234,7 @@ class _Problem:
         p.bias = _ptr(self.b32)
         p.event_order = _ptr(self.order)
         p.qkv_row_stride = self.qkv_row_stride
+        p.flags = _lib.FST_FLAG_SHARE_SMS if self.share_sms else 0
         return p
 
     def stat_shape(self) -> Tuple[int, ...]:
@@ -367,6 +370,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         use_activation_bias: bool,
         layout: str = "bhld",
         host_projection: bool = False,
+        share_sms: bool = False,
     ) -> Tensor:
         if feats.requires_grad:
             raise ValueError("feats (detector data) must not require grad")
@@ -375,7 +379,8 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         if k.dtype != q.dtype or v.dtype != q.dtype:
             raise ValueError("q, k and v must have the same dtype")
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
-                      use_attn_bias, use_activation_bias, layout, host_projection)
+                      use_attn_bias, use_activation_bias, layout, host_projection,
+                      share_sms=share_sms)
         qc, kc, vc = (_dense(t) for t in (q, k, v))
         out, lse = fused_forward(pb, qc, kc, vc)
         ctx.save_for_backward(qc, kc, vc, out, lse)
@@ -399,7 +404,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             g["dq"] if need[0] else None,
             g["dk"] if need[1] else None,
             g["dv"] if need[2] else None,
-            None, dw, db, None, None, None, None, None, None, None,
+            None, dw, db, None, None, None, None, None, None, None, None,
         )
 
 
@@ -419,6 +424,7 @@ def flash_spacetime_attention(
     layout: str = "bhld",
     validate_mask: bool = True,
     host_projection: bool = False,
+    share_sms: bool = False,
 ) -> Tensor:
     """Fused spacetime-bias attention on a padded batch (upstream forward.py:481-501).
 
@@ -440,6 +446,10 @@ def flash_spacetime_attention(
     ``w~ = dO W`` on the host in fp32, rounded once to q's dtype, as upstream
     does (forward.py:279-286, backward.py:546-547), and passes them to the
     kernels; by default the kernels form them in their prologue.
+    ``share_sms=True`` is a performance hint for callers that run another
+    kernel beside the op on every SM (a data loader's host-to-device copy of
+    the next batch on a side stream, ``upload_valid_rows``): the backward
+    then leaves room on each SM for it. Results do not depend on it.
     """
     length = q.shape[1] if layout == "blhd" else q.shape[2]
     if key_padding_mask is not None:
@@ -452,7 +462,7 @@ def flash_spacetime_attention(
         seqlens = seqlens_from_mask(seqlens, validate_mask)
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, seqlens, None,
-        scale, use_attn_bias, use_activation_bias, layout, host_projection,
+        scale, use_attn_bias, use_activation_bias, layout, host_projection, share_sms,
     )
 
 
@@ -469,17 +479,18 @@ def flash_spacetime_attention_varlen(
     use_activation_bias: bool = True,
     *,
     host_projection: bool = False,
+    share_sms: bool = False,
 ) -> Tensor:
     """Packed, uncapped variant (upstream forward.py:504-527).
 
     q, k, v: ``[T, H, Dh]``; feats ``[T, F]``; ``cu_seqlens`` ``[B+1]`` token
     offsets (cu[0] = 0, cu[-1] = T) -- the values buffer of a jagged
     NestedTensor. No padding exists and no host synchronisation happens.
-    ``host_projection`` as for :func:`flash_spacetime_attention`.
+    ``host_projection`` and ``share_sms`` as for :func:`flash_spacetime_attention`.
     """
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, None, cu_seqlens,
-        scale, use_attn_bias, use_activation_bias, "bhld", host_projection,
+        scale, use_attn_bias, use_activation_bias, "bhld", host_projection, share_sms,
     )
 
 

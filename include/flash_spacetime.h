@@ -105,7 +105,17 @@ typedef struct FstProblem {
    * reference.py:187-223). Must be a multiple of Dh and of 8 elements, and
    * >= H*Dh; 0 for the padded [B,H,L,D] layout. out, dout, u, wt stay dense. */
   int32_t qkv_row_stride;
+  /* FST_FLAG_* bits (performance hints; results do not depend on them). */
+  int32_t flags;
 } FstProblem;
+
+/* Another kernel runs beside this call on every SM -- typically the host to
+ * device gather of a training loop's next batch (fst_upload_rows on a side
+ * stream). The backward then uses kernel variants that leave registers free
+ * for it (its column kernel would otherwise fill each SM and serialise the
+ * two); about 7 % slower when nothing runs beside it. No upstream
+ * counterpart. */
+#define FST_FLAG_SHARE_SMS 1
 
 typedef struct FstForwardArgs {
   FstProblem prob;

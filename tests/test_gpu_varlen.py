@@ -336,3 +336,31 @@ def test_fused_qkv_matches_separate(packed, dtype):
     if not packed:
         for i, n in enumerate(lens):  # padding rows of out and of the fused gradient are 0
             assert torch.count_nonzero(res[1][0][i, n:]) == 0
+
+
+@pytest.mark.parametrize("packed", [False, True])
+def test_share_sms_hint_is_bitwise_neutral(packed):
+    # share_sms only selects kernel variants with a smaller register budget;
+    # the arithmetic is the same, so every output and gradient is bit-identical.
+    case = cs.padded_case(3, 90, 12, 32, 16, True, seed=919)
+    pk = cs.packed_from_padded(case)
+    dtype = torch.bfloat16
+    res = []
+    for share in (False, True):
+        if packed:
+            q, k, v = (_to(pk[x], dtype).requires_grad_(True) for x in ("q", "k", "v"))
+            w = _to(case["weight"], torch.float32).requires_grad_(True)
+            out = flash_spacetime_attention_varlen(q, k, v, pk["feats"].cuda(), w,
+                                                   _to(case["bias"], torch.float32),
+                                                   pk["cu"].cuda(), share_sms=share)
+            out.backward(_to(pk["grad"], dtype))
+        else:
+            q, k, v = (_to(case[x], dtype).requires_grad_(True) for x in ("q", "k", "v"))
+            w = _to(case["weight"], torch.float32).requires_grad_(True)
+            out = flash_spacetime_attention(q, k, v, case["feats"].cuda(), w,
+                                            _to(case["bias"], torch.float32),
+                                            case["seqlens"].cuda(), share_sms=share)
+            out.backward(_to(case["grad"], dtype))
+        res.append((out.detach(), q.grad, k.grad, v.grad, w.grad))
+    for a, b in zip(res[0], res[1]):
+        assert torch.equal(a, b)

@@ -21,11 +21,11 @@ events of length uniform in [2048, 16384], strong scaling).
 Under torchrun (N > 1) every rank owns a shard of the events chosen by
 longest-first L^2 balancing: N x 256 events for config1 (weak scaling:
 per-GPU work stays fixed), the fixed 2048 events of config4 (strong
-scaling). Inside the step the outputs of all ranks are all-gathered over
-NCCL (valid rows, packed; issued after the forward so that the transfer
-overlaps the backward) and the per-rank dW/db partials are gathered and
-summed in rank order; the step time is the max over ranks of the
-device-timed duration.
+scaling). Inside the step the per-rank dW/db partials are gathered and
+summed in rank order; for config4 (and with ``--gather-out``) the outputs
+of all ranks are also all-gathered over NCCL after the backward (valid rows,
+packed), as the sharded long-event run specifies. The step time is the max
+over ranks of the device-timed duration.
 
 Printed: one JSON line on rank 0 (see the keys below). ``value`` has inputs
 resident in HBM; ``e2e`` repeats the step with the inputs copied from pinned
@@ -356,6 +356,9 @@ def run_ours(args):
     else:
         data = synthetic.packed_batch(lens, heads, dim, channels, dtype, device,
                                       args.seed + 17 * rank, scaled)
+    # The generators' fp32 temporaries leave the caching allocator fragmented;
+    # config4 needs ~150 GB of one GPU's memory in large blocks.
+    torch.cuda.empty_cache()
     flops = synthetic.pair_flops(lens, heads, dim, channels)
     total_flops = sum(synthetic.pair_flops(x, heads, dim, channels)["total"] for x in per_rank)
 
@@ -369,7 +372,8 @@ def run_ours(args):
     # ([rows, Dh]; a padded batch's valid rows are gathered by a precomputed
     # index), with the row counts known on every rank from the partition.
     gather = None
-    if world > 1 and not args.no_gather:
+    want_gather = args.gather_out if args.gather_out is not None else args.workload == "config4"
+    if world > 1 and want_gather:
         if padlen is not None:
             sizes = [sum(x) * heads for x in per_rank]
             idx = torch.cat([(b * heads + h) * padlen + torch.arange(n)
@@ -378,6 +382,7 @@ def run_ours(args):
             sizes = [sum(x) * heads for x in per_rank]
             idx = None
         gather = RowGather(sizes, (dim,), dtype, device)
+    gather_timer = [] if gather is not None else None
 
     def step(lv, feats_, grad_, seq_or_cu, share_sms=False):
         for t in lv.values():
@@ -389,16 +394,26 @@ def run_ours(args):
             out = ops.flash_spacetime_attention_varlen(lv["q"], lv["k"], lv["v"], feats_,
                                                        lv["weight"], lv["bias"], seq_or_cu,
                                                        share_sms=share_sms)
-        work = None
+        out.backward(grad_)
         if gather is not None:
+            if gather_timer is not None:
+                g0 = torch.cuda.Event(enable_timing=True)
+                g0.record()
+            # After the backward, not overlapping it: NCCL's kernels wait on
+            # their peers while holding SMs, and next to the backward's SM-
+            # filling kernels that cost 0.42 ms a step on 2 GPUs instead of
+            # the ~0.1 ms the transfer takes on its own.
             rows = out.detach().view(-1, dim)
             n = gather.sizes[rank]
             if idx is not None:
                 torch.index_select(rows, 0, idx, out=gather.send[:n])
             else:
                 gather.send[:n].copy_(rows)
-            work = gather.start()  # overlaps the backward (NCCL's own stream)
-        out.backward(grad_)
+            gather.start().wait()
+            if gather_timer is not None:
+                g1 = torch.cuda.Event(enable_timing=True)
+                g1.record()
+                gather_timer.append((g0, g1))
         dw = lv["weight"].grad
         db = lv["bias"].grad
         if world > 1:
@@ -406,8 +421,6 @@ def run_ours(args):
             flat = ordered_sum(flat)
             dw = flat[: dw.numel()].view_as(dw)
             db = flat[dw.numel():]
-        if work is not None:
-            work.wait()
         return out, dw, db
 
     index = data["seqlens"] if padlen is not None else data["cu_seqlens"]
@@ -418,6 +431,8 @@ def run_ours(args):
         step(leaves, feats, grad, index)
     torch.cuda.synchronize()
     timers.clear()
+    if gather_timer is not None:
+        gather_timer.clear()
 
     torch.cuda.reset_peak_memory_stats(device)
     base_mem = torch.cuda.memory_allocated(device)
@@ -448,6 +463,8 @@ def run_ours(args):
     per = {}
     for name, e0, e1 in timers:
         per.setdefault(name, []).append(e0.elapsed_time(e1))
+    gather_ms = (statistics.mean(a.elapsed_time(b) for a, b in gather_timer)
+                 if gather_timer else None)
     fwd_ms = statistics.mean(per.get("fst_forward", [0.0]))
     bwd_ms = statistics.mean(per.get("fst_backward", [0.0]))
     value = total_flops / (ms * 1e-3) / 1e12
@@ -499,11 +516,11 @@ def run_ours(args):
                    "output_gather": (None if gather is None else
                                      f"all_gather_into_tensor of every rank's valid output rows, "
                                      f"{gather.bytes_received() / 1e6:.0f} MB received per rank "
-                                     f"per step, overlapping the backward"),
+                                     f"per step, after the backward"),
                    "l2_policy": f"inputs larger than L2 (q, k, v, grad "
                                 f"{data['q'].numel() * data['q'].element_size() / 1e6:.0f} MB "
                                 f"each)"},
-        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "peak_gib": peak_gib,
+        "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "gather_ms": gather_ms, "peak_gib": peak_gib,
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,
@@ -530,7 +547,10 @@ def main():
     ap.add_argument("--dtype", default="bf16", choices=("bf16", "fp16"), help="config2 dtype")
     ap.add_argument("--events", type=int, default=0,
                     help="config1 events per GPU (default 256; smaller for profiler captures)")
-    ap.add_argument("--no-gather", action="store_true",
+    ap.add_argument("--gather-out", dest="gather_out", action="store_true", default=None,
+                    help="multi-GPU: all-gather every rank's outputs inside the step "
+                         "(the default for config4, whose sharded run names it)")
+    ap.add_argument("--no-gather", dest="gather_out", action="store_false",
                     help="multi-GPU: skip the all-gather of the outputs")
     ap.add_argument("--coords", default="raw", choices=("raw", "scaled"))
     ap.add_argument("--seed", type=int, default=2026)
@@ -542,6 +562,11 @@ def main():
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
+    if args.workload == "config4":
+        # ~150 GB of one GPU in large blocks that are freed and re-taken every
+        # step; expandable segments keep the caching allocator from
+        # fragmenting (read when CUDA initialises, which has not happened yet).
+        os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
     if args.impl == "reference":
         run_reference(args)
     else:

@@ -131,7 +131,9 @@ class ClockSampler:
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, device: int):
+        import threading
         self.proc = None
+        self.lines = []
         try:
             uuid = str(torch.cuda.get_device_properties(device).uuid)
             ident = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
@@ -139,18 +141,27 @@ class ClockSampler:
                 ["nvidia-smi", "-i", ident, f"--query-gpu={self.FIELDS}",
                  "--format=csv,noheader,nounits", "-lms", "50"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            # Drain the pipe as samples arrive: a long run fills the pipe's
+            # buffer otherwise, and nvidia-smi stops sampling.
+            self.reader = threading.Thread(target=self._drain, daemon=True)
+            self.reader.start()
         except Exception:
             self.proc = None
+
+    def _drain(self):
+        for line in self.proc.stdout:
+            self.lines.append(line)
 
     def stop(self, t0: float, t1: float):
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"]}
         self.proc.terminate()
         try:
-            out, _ = self.proc.communicate(timeout=10)
+            self.proc.wait(timeout=10)
+            self.reader.join(timeout=10)
         except Exception:
             self.proc.kill()
-            out = ""
+        out = "".join(self.lines)
         import datetime
         names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
         samples = []

@@ -632,9 +632,12 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   if constexpr (!S::kFits) {
     return FST_ERR_UNSUPPORTED;
   } else {
-    const bool shared = has_shared_variant<DH, C>() && (p.flags & FST_FLAG_SHARE_SMS);
-    const void* fn = shared ? (const void*)bwd_cols_tc_shared_kernel<T, DH, C>
-                            : (const void*)bwd_cols_tc_kernel<T, DH, C>;
+    bool shared = false;
+    const void* fn = (const void*)bwd_cols_tc_kernel<T, DH, C>;
+    if constexpr (has_shared_variant<DH, C>()) {
+      shared = (p.flags & FST_FLAG_SHARE_SMS) != 0;
+      if (shared) fn = (const void*)bwd_cols_tc_shared_kernel<T, DH, C>;
+    }
     static std::atomic<uint64_t> configured{0}, configured_shared{0};
     if (allow_dynamic_smem(fn, S::SMEM, shared ? configured_shared : configured))
       return FST_ERR_CUDA;
@@ -650,12 +653,16 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
       grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
     }
     if (grid.x == 0 || grid.y == 0) return FST_OK;
-    if (shared)
-      bwd_cols_tc_shared_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
-          a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
-    else
-      bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
-          a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
+    if constexpr (has_shared_variant<DH, C>()) {
+      if (shared) {
+        bwd_cols_tc_shared_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
+            a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
+        count_launch();
+        return FST_OK;
+      }
+    }
+    bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
+        a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
     count_launch();
     return FST_OK;
   }

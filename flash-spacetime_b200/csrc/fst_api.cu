@@ -100,6 +100,15 @@ int check_tc_alignment(const FstProblem& p, std::initializer_list<const void*> p
   return FST_OK;
 }
 
+// A launch helper that failed has already recorded why; keep that text
+// behind the entry point's own prefix.
+int launch_fail(int code, const char* what) {
+  char inner[sizeof(g_err)];
+  strncpy(inner, g_err, sizeof(inner) - 1);
+  inner[sizeof(inner) - 1] = '\0';
+  return fail(code, "%s launch failed: %s", what, inner[0] ? inner : "(no detail)");
+}
+
 int cuda_status(const char* where) {
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return fail(FST_ERR_CUDA, "%s: %s", where, cudaGetErrorString(e));
@@ -169,12 +178,13 @@ int fst_forward(const FstForwardArgs* a, void* stream) {
     if (rc) return rc;
   }
   cudaGetLastError();  // clear a stale error so the check below is ours
+  g_err[0] = '\0';
   if (fst::tc::fwd_supported(p)) {
     rc = fst::tc::launch_fwd(*a, (cudaStream_t)stream);
   } else {
     rc = fst::simt::launch_fwd(*a, (cudaStream_t)stream);
   }
-  if (rc) return fail(rc, "forward launch failed");
+  if (rc) return launch_fail(rc, "forward");
   return cuda_status("forward launch");
 }
 
@@ -200,11 +210,12 @@ int fst_backward(const FstBackwardArgs* a, void* stream) {
     if (rc) return rc;
   }
   cudaGetLastError();
+  g_err[0] = '\0';
   if (fst::tc::bwd_supported(p))
     rc = fst::tc::launch_bwd(*a, (cudaStream_t)stream);
   else
     rc = fst::simt::launch_bwd(*a, (cudaStream_t)stream);
-  if (rc) return fail(rc, "backward launch failed");
+  if (rc) return launch_fail(rc, "backward");
   return cuda_status("backward launch");
 }
 

@@ -1,6 +1,7 @@
 // Internal declarations shared by the C-ABI front end and the kernel files.
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 #include <atomic>
@@ -23,6 +24,11 @@ size_t bwd_workspace(const FstProblem& p);
 int64_t dw_parts(const FstProblem& p);
 }  // namespace simt
 namespace tc {
+// TMA tensor map of a 16-bit [*, H, Dh]-addressed tensor of problem p (the 2D
+// row view described in fst_tma.cu); row_elems is its row stride in elements
+// for the row-interleaved layouts. Only Dh in {16, 32, 64} (tma_shape).
+bool tma_shape(int dh);
+int make_head_map(CUtensorMap* map, const FstProblem& p, const void* base, int row_elems);
 bool fwd_supported(const FstProblem& p);
 size_t fwd_workspace(const FstProblem& p);
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);

@@ -56,8 +56,12 @@ struct ColShape {
   static constexpr int JS = 32;
   static constexpr int HS = BK * JS + 8;
   static constexpr int SZ_BIAS = HP * HS * 4;                 // one stage
-  // head-warp ring stage: Q chunk, dO chunk [BQ][DHP] + LSE, D [BQ]
-  static constexpr int SZ_HR = 2 * BQ * RBD + 2 * BQ * 4;
+  // head-warp ring stage: qt chunk, dO chunk [BQ][DHP] by cp.async, and their
+  // LSE and D [BQ] in a separate stats ring. (A TMA ring for the tiles, as in
+  // the forward and row kernels, doubled this kernel's spills at 128
+  // registers a thread and measured 7 % slower on config 1: 1124 vs 1049 us.)
+  static constexpr int SZ_HR = 2 * BQ * RBD;
+  static constexpr int SZ_HS = 2 * BQ * 4;
   // E-warp ring stage: u and w~ rows [QPE][HP][CP] + query coords [QPE][4].
   // The MMA's head rows past the CTA's heads read a shared zero row instead.
   static constexpr int UW = QPE * HP * RBC;                   // one of u / w~
@@ -67,8 +71,9 @@ struct ColShape {
   static constexpr int OFF_KS = 0, OFF_VS = SZ_KVS;           // prologue only
   static constexpr int OFF_BIAS = 0;                          // loop: [2][HP][BK][JS]
   static constexpr int SZ_U = (2 * SZ_KVS > 2 * SZ_BIAS) ? 2 * SZ_KVS : 2 * SZ_BIAS;
-  static constexpr int OFF_HR = SZ_U;                         // [HP][2] stages
-  static constexpr int OFF_ER = OFF_HR + HP * 2 * SZ_HR;      // [NE][2] stages
+  static constexpr int OFF_HR = SZ_U;                         // [HP][2] tile stages
+  static constexpr int OFF_HS = OFF_HR + HP * 2 * SZ_HR;      // [HP][2] LSE, D stages
+  static constexpr int OFF_ER = OFF_HS + HP * 2 * SZ_HS;      // [NE][2] stages
   static constexpr int OFF_KC = OFF_ER + NE * 2 * SZ_ER;      // key coords [BK][4]
   static constexpr int OFF_ZR = OFF_KC + BK * 16;             // zero row [CP]
   static constexpr int SMEM = OFF_ZR + RBC;
@@ -382,15 +387,17 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   const int hl = warp;
   const int h = h0 + hl;
   const uint32_t ring = sm + S::OFF_HR + hl * 2 * S::SZ_HR;
-  const T* __restrict__ qbase = gqt + ev_off(ev, 0, h, DH);  // qt = [q * scale]
-  const T* __restrict__ dobase = gdo + ev_off(ev, 0, h, DH);
-  const int rs = row_stride(p, DH);
+  const uint32_t sring = sm + S::OFF_HS + hl * 2 * S::SZ_HS;
   const float* __restrict__ lse_h = a.lse + ev_off(ev, 0, h, 1);  // row qi at qi * ev.rs1
   const float* __restrict__ delta_h = a.delta + ev_off(ev, 0, h, 1);
   auto load_ring = [&](int n) {
     if (n < nchunks) {
       const uint32_t st = ring + (n & 1) * S::SZ_HR;
       constexpr int CH = DH / 8;
+      // qt = [q * scale] and dO of this head: event base pointers and row stride.
+      const T* __restrict__ qbase = gqt + ev_off(ev, 0, h, DH);
+      const T* __restrict__ dobase = gdo + ev_off(ev, 0, h, DH);
+      const int rs = row_stride(p, DH);
       for (int idx = lane; idx < S::BQ * CH; idx += 32) {
         const int c = idx % CH, i = idx / CH;
         const uint32_t off = swz<S::RBD>(i, c);
@@ -407,7 +414,7 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
       }
       if (lane < S::BQ) {  // LSE (natural log) and D of the chunk's queries
         const int qi = n * S::BQ + lane;
-        const uint32_t f = st + 2 * S::BQ * S::RBD + lane * 4;
+        const uint32_t f = sring + (n & 1) * S::SZ_HS + lane * 4;
         if (qi < ev.len) {
           cp_async4(f, lse_h + qi * ev.rs1);
           cp_async4(f + S::BQ * 4, delta_h + qi * ev.rs1);
@@ -440,11 +447,11 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   // One query chunk; the stage s = n & 1 is passed as a literal.
   auto step = [&](int n, int s) {
     const int i0 = n * S::BQ;
-    cp_async_wait<1>();
-    __syncwarp();
     const uint32_t st = ring + s * S::SZ_HR;
     const uint32_t q_st = st, do_st = st + S::BQ * S::RBD;
-    const float* stat = (const float*)(smem + (st - sm) + 2 * S::BQ * S::RBD);
+    const float* stat = (const float*)(smem + (sring - sm) + s * S::SZ_HS);
+    cp_async_wait<1>();
+    __syncwarp();
 
     // S^T = K Q^T, dP^T = V dO^T (B fragments: k = head dim, n = query).
     float sc[2][4], dp[2][4];
@@ -576,7 +583,6 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   } else {
     for (int n = 0; n < nchunks; ++n) step(n, n & 1);
   }
-
 #pragma unroll
   for (int rh = 0; rh < 2; ++rh) {
     const int j = r8 + 8 * rh;
@@ -640,7 +646,7 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
     }
     static std::atomic<uint64_t> configured{0}, configured_shared{0};
     if (allow_dynamic_smem(fn, S::SMEM, shared ? configured_shared : configured))
-      return FST_ERR_CUDA;
+      return api_fail(FST_ERR_CUDA, "cannot allow %d bytes of dynamic shared memory", S::SMEM);
     const int groups = (p.heads + S::HP - 1) / S::HP;
     const int per_group = (p.heads + groups - 1) / groups;
     const int threads = (per_group + S::NE) * 32;

@@ -88,7 +88,10 @@ struct RowShape {
   static constexpr int OFF_H = 0, OFF_G = BM * HP * C * 4;
   static constexpr int OFF_W = SZ_UNION;
   static constexpr int SZ_W = 2 * DH * RBC;
-  static constexpr int OFF_K = OFF_W + SZ_W;
+  // K / V rings come by TMA where the box (16 rows x Dh) fills whole swizzled
+  // rows (Dh = 16, 32, 64); their stages start on 1024-byte boundaries.
+  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64);
+  static constexpr int OFF_K = (OFF_W + SZ_W + 1023) / 1024 * 1024;
   static constexpr int SZ_KV = HP * BN * RBD;
   static constexpr int OFF_V = OFF_K + 2 * SZ_KV;
   static constexpr int OFF_C = OFF_V + 2 * SZ_KV;           // [NE][2][BN][4]
@@ -104,8 +107,9 @@ struct RowShape {
   // offsets are staged in the union region next to the scaled Q.
   static constexpr int OFF_QR = END_UW, OFF_DOR = OFF_QR + SZ_QS;
   static constexpr int OFF_OS = SZ_QS;
-  static constexpr bool FASTPRO = AHEAD && OFF_DOR + SZ_QS <= 227 * 1024;
-  static constexpr int SMEM = FASTPRO ? OFF_DOR + SZ_QS : END_UW;
+  static constexpr bool FASTPRO = AHEAD && OFF_DOR + SZ_QS + HP * 16 <= 227 * 1024;
+  static constexpr int OFF_MB = FASTPRO ? OFF_DOR + SZ_QS : END_UW;  // ring mbarriers [HP][2]
+  static constexpr int SMEM = OFF_MB + HP * 16;
   static_assert(!FASTPRO || 2 * SZ_QS <= OFF_P, "staged Q / out do not overlap the P tiles");
   static constexpr int OFF_R = OFF_K;                        // [BM][HP][DH] fp32
   static_assert(BM * HP * DH * 4 <= 4 * SZ_KV, "R fits the K/V ring");
@@ -122,10 +126,10 @@ template <typename T, int DH, int C>
 __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     bwd_rows_tc_kernel(const FstBackwardArgs a, const int* __restrict__ tile_start,
                        int heads_per_group, T* __restrict__ u_ws, T* __restrict__ wt_ws,
-                       T* __restrict__ qt_ws) {
+                       T* __restrict__ qt_ws, const __grid_constant__ TmaPair kv_maps) {
   using S = RowShape<DH, C>;
   using E = Elem<T>;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem[];
   const FstProblem& p = a.prob;
 
   int b, qb;
@@ -720,13 +724,39 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     const int h = h0 + hl;
     const uint32_t k_ring = sm + S::OFF_K + hl * S::BN * S::RBD;
     const uint32_t v_ring = sm + S::OFF_V + hl * S::BN * S::RBD;
-    // K / V of this head: event base pointer and row stride (no 64-bit math
-    // per copy).
-    const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
-    const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
-    const int rs = qkv_row_stride(p, DH);
+    // TMA ring (as in the forward): one mbarrier per stage; the box origin is
+    // this head's first column and the event's row of key 0 in the row view.
+    const uint32_t mbar = sm + S::OFF_MB + hl * 16;
+    const int tx = rows_interleaved(p) ? h * DH : 0;
+    const int ty = rows_interleaved(p) ? (int)evq.row0 : (int)(evq.base1 + h * evq.hs1);
+    bool tma_late = false;
+    const bool ring_tma = S::TMA && ((sm + S::OFF_K) & 1023u) == 0;
+    if (ring_tma) {
+      if (lane == 0) {
+        mbar_init(mbar, 1);
+        mbar_init(mbar + 8, 1);
+        mbar_init_fence();
+      }
+      __syncwarp();
+    }
     auto load_kv = [&](int n) {
+      if (ring_tma) {
+        if (n < nchunks && lane == 0) {
+          const int st = n & 1;
+          const uint32_t bar = mbar + 8 * st;
+          fence_proxy_async();
+          mbar_arrive_tx(bar, 2 * S::BN * DH * (int)sizeof(T));
+          tma_load_2d(k_ring + st * S::SZ_KV, &kv_maps.a, bar, tx, ty + n * S::BN);
+          tma_load_2d(v_ring + st * S::SZ_KV, &kv_maps.b, bar, tx, ty + n * S::BN);
+        }
+        return;
+      }
       if (n < nchunks) {
+        // K / V of this head: event base pointer and row stride (formed here,
+        // so they hold no registers across the TMA path's loop).
+        const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
+        const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
+        const int rs = qkv_row_stride(p, DH);
         constexpr int CH = DH / 8;
         const int j0 = n * S::BN;
         const uint32_t ks_ = k_ring + (n & 1) * S::SZ_KV, vs_ = v_ring + (n & 1) * S::SZ_KV;
@@ -764,9 +794,23 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     // One key chunk; the stage s = n & 1 is passed as a literal.
     auto step = [&](int n, int s) {
       const int j0 = n * S::BN;
-      cp_async_wait<1>();
-      __syncwarp();
       const uint32_t k_st = k_ring + s * S::SZ_KV, v_st = v_ring + s * S::SZ_KV;
+      if (ring_tma) {
+        if (!mbar_wait(mbar + 8 * s, (n >> 1) & 1)) tma_late = true;
+        if (j0 + S::BN > ev.len) {  // keys past the event must be exact zeros
+          constexpr int CH = DH / 8;
+          for (int idx = lane; idx < S::BN * CH; idx += 32) {
+            const int c = idx % CH, j = idx / CH;
+            if (j0 + j >= ev.len) {
+              asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(k_st + swz<S::RBD>(j, c)), "r"(0));
+              asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(v_st + swz<S::RBD>(j, c)), "r"(0));
+            }
+          }
+        }
+      } else {
+        cp_async_wait<1>();
+      }
+      __syncwarp();
       // S = Q K^T and dP = dO V^T (B fragments: k = head dim, n = key).
       float sc[2][4], dp[2][4];
 #pragma unroll
@@ -889,6 +933,17 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     } else {
       for (int n = 0; n < nchunks; ++n) step(n, n & 1);
     }
+    if (ring_tma) {
+      // A ring wait that gave up leaves its copy in flight: wait (bounded) for
+      // the last copy of each stage before the ring is reused, and flag this
+      // warp's rows (delta = NaN) below.
+      tma_late = __any_sync(0xffffffffu, tma_late);
+      if (tma_late)
+        for (int st = 0; st < 2 && st < nchunks; ++st) {
+          const int last = nchunks - 1 - ((nchunks - 1 - st) & 1);
+          mbar_wait(mbar + 8 * st, (last >> 1) & 1);
+        }
+    }
 
     // D' = a / p, sigma = a - D' p, dqp = X - D' Y (rows r8 and r8 + 8).
     float dpr[2], sig[2];
@@ -933,7 +988,9 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
       }
       if (m4 == 0) {
         const int64_t so = ev_off(ev, q0 + q, h, 1);
-        a.delta[so] = valid ? fCoff[q * S::HP + hl] + dpr[rh] : 0.f;
+        a.delta[so] = tma_late ? __int_as_float(0x7fc00000)  // a K/V copy never landed
+                      : valid  ? fCoff[q * S::HP + hl] + dpr[rh]
+                               : 0.f;
         a.sigma[so] = valid ? sig[rh] : 0.f;
       }
     }
@@ -1056,15 +1113,22 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   }
   static std::atomic<uint64_t> configured{0};
   if (allow_dynamic_smem((const void*)bwd_rows_tc_kernel<T, DH, C>, S::SMEM, configured))
-    return FST_ERR_CUDA;
+    return api_fail(FST_ERR_CUDA, "cannot allow %d bytes of dynamic shared memory", S::SMEM);
+  TmaPair maps{};
+  if constexpr (S::TMA) {
+    const int rs = p.qkv_row_stride ? p.qkv_row_stride : p.heads * DH;
+    int rc = make_head_map(&maps.a, p, a.k, rs);
+    if (!rc) rc = make_head_map(&maps.b, p, a.v, rs);
+    if (rc) return rc;
+  }
   const dim3 grid = rows_grid<DH, C>(p);
   const int groups = (int)grid.z;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;
   if (is_varlen(p)) tile_prefix(p, S::BM, tile_start, st);
   if (grid.x == 0 || grid.y == 0) return FST_OK;
-  bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group,
-                                                                 (T*)u_ws, (T*)wt_ws, (T*)qt_ws);
+  bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
+      a, tile_start, per_group, (T*)u_ws, (T*)wt_ws, (T*)qt_ws, maps);
   count_launch();
   return FST_OK;
 }

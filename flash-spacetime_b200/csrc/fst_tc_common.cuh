@@ -3,6 +3,7 @@
 // the sin/cos of the pair embedding and the tensor-core projection.
 #pragma once
 
+#include <cuda.h>  // CUtensorMap (the type only; maps are encoded on the host)
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <stdint.h>
@@ -11,6 +12,16 @@
 
 namespace fst {
 namespace tc {
+
+// The two TMA tensor maps a kernel streams per head: K and V (forward, row
+// kernel) or qt and dO (column kernel). Each describes a 2D row view of a
+// 16-bit tensor -- [B*H*L, Dh] for the padded layout, [rows, H*Dh] (row
+// stride as given) for the row-interleaved ones -- with a [16 rows x Dh] box
+// and the shared-memory swizzle that equals swz<Dh * 2> below. Passed by
+// value as a __grid_constant__ kernel parameter.
+struct __align__(64) TmaPair {
+  CUtensorMap a, b;
+};
 
 // ---- element types ---------------------------------------------------------
 
@@ -140,6 +151,55 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
 }
 __device__ __forceinline__ void named_arrive(int id, int nthreads) {
   asm volatile("bar.arrive %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// ---- mbarriers and TMA (cp.async.bulk.tensor) -------------------------------
+
+__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(bar), "r"(count) : "memory");
+}
+// Makes initialised barriers visible to the async proxy (the TMA unit).
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+}
+// One arrival that also expects `bytes` of TMA transactions on this phase.
+__device__ __forceinline__ void mbar_arrive_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+// Waits for the phase of parity `parity` to complete, giving up after a
+// bounded number of polls (each try_wait itself suspends for a while), so a
+// transfer that never lands cannot hang the GPU. Returns false on give-up.
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
+  for (int i = 0; i < (1 << 22); ++i)
+    if (mbar_test(bar, parity)) return true;
+  return false;
+}
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// its later async-proxy (TMA) writes to it.
+__device__ __forceinline__ void fence_proxy_async() {
+  asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+}
+// 2D tiled TMA load of the box at (x = column, y = row) of `map` into `dst`,
+// completing `bar`'s transaction count. x * 2 bytes is a multiple of 16 (x is
+// a multiple of Dh); rows past the tensor's end read as zeros.
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar,
+                                            int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];\n" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
 }
 
 // ---- math ------------------------------------------------------------------

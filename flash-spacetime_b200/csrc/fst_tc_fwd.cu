@@ -108,14 +108,19 @@ struct FwdShape {
   static constexpr int OFF_A = OFF_P + 2 * SZ_P;              // alpha [2][BM][HP]
   static constexpr int OFF_W = SZ_UNION;                      // W hi, W lo: [DH][CP]
   static constexpr int SZ_W = 2 * DH * RBC;
-  static constexpr int OFF_K = OFF_W + SZ_W;
+  // K / V rings come by TMA where the box (16 rows x Dh) fills whole swizzled
+  // rows (Dh = 16, 32, 64); their stages start on 1024-byte boundaries, as
+  // the TMA swizzle patterns (32/64/128 B) require.
+  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64);
+  static constexpr int OFF_K = (OFF_W + SZ_W + 1023) / 1024 * 1024;
   static constexpr int SZ_KV = HP * BN * RBD;                 // one stage of K (or V)
   static constexpr int OFF_V = OFF_K + 2 * SZ_KV;
   static constexpr int OFF_C = OFF_V + 2 * SZ_KV;             // key coords [NE][2][BN][4]
   static constexpr int OFF_QC = OFF_C + NE * 2 * BN * 16;     // query coords [BM][4]
   static constexpr int OFF_L = OFF_QC + BM * 16;              // row sums [BM][HP]
   static constexpr int OFF_F = OFF_L + BM * HP * 4;           // rescale flags [2][16] int
-  static constexpr int SMEM = OFF_F + 2 * 16 * 4;
+  static constexpr int OFF_MB = OFF_F + 2 * 16 * 4;           // K/V ring mbarriers [HP][2]
+  static constexpr int SMEM = OFF_MB + HP * 16;
   // Whether the P tiles lie clear of the staging bytes (then they are zeroed
   // while Q and u are staged, saving a barrier).
   static constexpr bool P_CLEAR = OFF_P >= SZ_STAGE;
@@ -152,10 +157,11 @@ __device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_st
 
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
-    fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group) {
+    fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group,
+                  const __grid_constant__ TmaPair kv_maps) {
   using S = FwdShape<DH, C>;
   using E = Elem<T>;
-  extern __shared__ __align__(128) unsigned char smem[];
+  extern __shared__ __align__(1024) unsigned char smem[];
   const FstProblem& p = a.prob;
 
   int b, qb;
@@ -546,13 +552,42 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     const int hl = warp;  // local head
     const int h = h0 + hl;
     // Private ring of this head's K and V chunks: [2 stages][BN][DHP].
-    // K / V of this head: event base pointer and row stride (no 64-bit math
-    // per copy).
-    const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
-    const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
-    const int rs = qkv_row_stride(p, DH);
+    // TMA ring: one mbarrier per stage; box (x = this head's first column,
+    // y = the event's row index of key 0 in the 2D row view).
+    const uint32_t mbar = sm + S::OFF_MB + hl * 16;
+    const int tx = rows_interleaved(p) ? h * DH : 0;
+    const int ty = rows_interleaved(p) ? (int)evq.row0 : (int)(evq.base1 + h * evq.hs1);
+    bool tma_late = false;  // a ring wait gave up (the copy never landed)
+    // The swizzled TMA boxes need their stages on 1024-byte boundaries of the
+    // shared window; the copy ring falls back to cp.async otherwise.
+    const bool ring_tma = S::TMA && (sK & 1023u) == 0;
+    if (ring_tma) {
+      if (lane == 0) {
+        mbar_init(mbar, 1);
+        mbar_init(mbar + 8, 1);
+        mbar_init_fence();
+      }
+      __syncwarp();
+    }
     auto load_kv = [&](int n) {
+      if (ring_tma) {
+        if (n < nchunks && lane == 0) {
+          const int st = n & 1;
+          const uint32_t bar = mbar + 8 * st;
+          const uint32_t off = st * S::SZ_KV + hl * S::BN * S::RBD;
+          fence_proxy_async();  // the stage's earlier reads precede the async writes
+          mbar_arrive_tx(bar, 2 * S::BN * DH * (int)sizeof(T));
+          tma_load_2d(sK + off, &kv_maps.a, bar, tx, ty + n * S::BN);
+          tma_load_2d(sV + off, &kv_maps.b, bar, tx, ty + n * S::BN);
+        }
+        return;
+      }
       if (n < nchunks) {
+        // K / V of this head: event base pointer and row stride (formed here,
+        // so they hold no registers across the TMA path's loop).
+        const T* __restrict__ kbase = gk + ev_off(evq, 0, h, DH);
+        const T* __restrict__ vbase = gv + ev_off(evq, 0, h, DH);
+        const int rs = qkv_row_stride(p, DH);
         constexpr int CH = DH / 8;
         const int j0 = n * S::BN;
         const uint32_t k_st = sK + (n & 1) * S::SZ_KV + hl * S::BN * S::RBD;
@@ -591,10 +626,26 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     // offset folds into the shared-memory instructions.
     auto step = [&](int n, int s) {
       const int j0 = n * S::BN;
-      cp_async_wait<1>();
-      __syncwarp();
       const uint32_t k_st = sK + s * S::SZ_KV + hl * S::BN * S::RBD;
       const uint32_t v_st = sV + s * S::SZ_KV + hl * S::BN * S::RBD;
+      if (ring_tma) {
+        if (!mbar_wait(mbar + 8 * s, (n >> 1) & 1)) tma_late = true;
+        if (j0 + S::BN > ev.len) {
+          // Keys past the event: the box brought whatever lies there (the
+          // next event's rows or padding); they must be exact zeros.
+          constexpr int CH = DH / 8;
+          for (int idx = lane; idx < S::BN * CH; idx += 32) {
+            const int c = idx % CH, j = idx / CH;
+            if (j0 + j >= ev.len) {
+              asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(k_st + swz<S::RBD>(j, c)), "r"(0));
+              asm volatile("st.shared.v4.u32 [%0], {%1,%1,%1,%1};\n" ::"r"(v_st + swz<S::RBD>(j, c)), "r"(0));
+            }
+          }
+        }
+      } else {
+        cp_async_wait<1>();
+      }
+      __syncwarp();
 
       // K B-fragments (k = head dim, n = key): kb[nt][ks][2].
       uint32_t kb[2][S::KSD][2];
@@ -765,6 +816,17 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     } else {
       for (int n = 0; n < nchunks; ++n) step(n, n & 1);
     }
+    if (ring_tma) {
+      // A ring wait that gave up leaves its copy in flight: wait (bounded) for
+      // the last copy of each stage before the shared memory is released, and
+      // flag this warp's rows (lse = NaN) below.
+      tma_late = __any_sync(0xffffffffu, tma_late);
+      if (tma_late)
+        for (int st = 0; st < 2 && st < nchunks; ++st) {
+          const int last = nchunks - 1 - ((nchunks - 1 - st) & 1);
+          mbar_wait(mbar + 8 * st, (last >> 1) & 1);
+        }
+    }
 
     // Row sums over the quad, published for the E warps' A' normalisation.
 #pragma unroll
@@ -807,7 +869,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         }
         if (m4 == 0)
           a.lse[ev_off(ev, q0 + q, h, 1)] =
-              valid ? (mrun[rg][rh] + __log2f(lrun[rg][rh])) * 0.6931471805599453f : 0.f;
+              tma_late ? __int_as_float(0x7fc00000)  // a K/V copy never landed
+              : valid  ? (mrun[rg][rh] + __log2f(lrun[rg][rh])) * 0.6931471805599453f
+                       : 0.f;
       }
     return;
   }
@@ -865,9 +929,16 @@ template <typename T, int DH, int C>
 static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_start) {
   using S = FwdShape<DH, C>;
   const FstProblem& p = a.prob;
+  TmaPair maps{};
+  if constexpr (S::TMA) {
+    const int rs = p.qkv_row_stride ? p.qkv_row_stride : p.heads * DH;
+    int rc = make_head_map(&maps.a, p, a.k, rs);
+    if (!rc) rc = make_head_map(&maps.b, p, a.v, rs);
+    if (rc) return rc;
+  }
   static std::atomic<uint64_t> configured{0};  // per template instance, one bit per device
   if (allow_dynamic_smem((const void*)fwd_tc_kernel<T, DH, C>, S::SMEM, configured))
-    return FST_ERR_CUDA;
+    return api_fail(FST_ERR_CUDA, "cannot allow %d bytes of dynamic shared memory", S::SMEM);
   const int groups = (p.heads + S::HP - 1) / S::HP;
   const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
   const int threads = (per_group + S::NE) * 32;
@@ -880,7 +951,7 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
     grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
   }
   if (grid.x == 0 || grid.y == 0) return FST_OK;
-  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group);
+  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, maps);
   count_launch();
   return FST_OK;
 }

@@ -35,9 +35,14 @@ template <int DH, int C>
 struct ColShape {
   static constexpr int BK = 16;   // keys per CTA
   static constexpr int BQ = 16;   // queries per chunk
-  static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1);
+  // Queries per E warp and heads per CTA: 8 heads from C = 32 on, and two
+  // queries per E warp at (64, 64), keep 128 registers a thread (spills at
+  // (64, 64): 68 bytes instead of 568; config 2 measured 30.6 instead of
+  // 28.8 TFLOP/s). At (32, 64) one query per E warp stays faster (28.8 vs
+  // 27.2) despite its spills: the E side needs the extra warps there.
+  static constexpr int QPE = C <= 16 ? 4 : ((C <= 32 || DH >= 64) ? 2 : 1);
   static constexpr int NE = BQ / QPE;
-  static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;
+  static constexpr int HP = (DH <= 32 && C <= 16) ? 12 : 8;
   static constexpr int NWARPS = HP + NE;
   // Loops unrolled by two chunks with literal ring stages where the
   // registers allow it (the wide shapes would spill).

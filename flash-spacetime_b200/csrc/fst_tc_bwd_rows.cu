@@ -48,7 +48,10 @@ struct RowShape {
   // scheduler.
   static constexpr int QPE = C <= 32 ? 2 : 1;
   static constexpr int NE = BM / QPE;
-  static constexpr int HP = (DH <= 32 && C <= 32) ? 12 : 8;  // heads per CTA
+  // Heads per CTA: 12 only for the narrowest shapes; with C >= 32 a CTA of 8
+  // heads keeps 128 registers a thread (at C = 32: 116 bytes of spills
+  // instead of 368 with 12 heads at 96 registers).
+  static constexpr int HP = (DH <= 32 && C <= 16) ? 12 : 8;
   // E warps run one chunk ahead (two E fragments live). Their u / w~
   // A-fragments are then re-read from a resident staged tile each chunk
   // instead of being held in registers.
@@ -90,7 +93,10 @@ struct RowShape {
   static constexpr int SZ_W = 2 * DH * RBC;
   // K / V rings come by TMA where the box (16 rows x Dh) fills whole swizzled
   // rows (Dh = 16, 32, 64); their stages start on 1024-byte boundaries.
-  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64);
+  // At C = 64 the ring's barrier state costs the kernel registers it cannot
+  // spare (config 2 measured 27.4 / 30.6 TFLOP/s with TMA against 28.5 / 31.5
+  // with cp.async at Dh = 32 / 64), so those shapes keep cp.async.
+  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64) && C <= 32;
   static constexpr int OFF_K = (OFF_W + SZ_W + 1023) / 1024 * 1024;
   static constexpr int SZ_KV = HP * BN * RBD;
   static constexpr int OFF_V = OFF_K + 2 * SZ_KV;

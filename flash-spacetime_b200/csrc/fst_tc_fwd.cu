@@ -55,7 +55,10 @@ constexpr float kLazyMax = 8.f;
 
 template <int DH, int C>
 struct FwdShape {
-  static constexpr int BM = (DH <= 32 && C <= 32) ? 32 : 16;  // query rows per CTA
+  // 32 query rows per CTA only for the narrowest shapes: at C = 32 the
+  // 16-row block keeps 96 registers a thread (4 bytes of spills instead of
+  // 352 with 32 rows at 72 registers).
+  static constexpr int BM = (DH <= 32 && C <= 16) ? 32 : 16;  // query rows per CTA
   static constexpr int RG = BM / 16;                          // 16-row groups
   static constexpr int BN = 16;                               // keys per chunk
   static constexpr int QPE = C <= 16 ? 4 : (C <= 32 ? 2 : 1); // queries per E warp
@@ -111,7 +114,10 @@ struct FwdShape {
   // K / V rings come by TMA where the box (16 rows x Dh) fills whole swizzled
   // rows (Dh = 16, 32, 64); their stages start on 1024-byte boundaries, as
   // the TMA swizzle patterns (32/64/128 B) require.
-  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64);
+  // At C = 64 the ring's barrier state costs the kernel registers it cannot
+  // spare (config 2 measured 27.4 / 30.6 TFLOP/s with TMA against 28.5 / 31.5
+  // with cp.async at Dh = 32 / 64), so those shapes keep cp.async.
+  static constexpr bool TMA = (DH == 16 || DH == 32 || DH == 64) && C <= 32;
   static constexpr int OFF_K = (OFF_W + SZ_W + 1023) / 1024 * 1024;
   static constexpr int SZ_KV = HP * BN * RBD;                 // one stage of K (or V)
   static constexpr int OFF_V = OFF_K + 2 * SZ_KV;

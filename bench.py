@@ -395,12 +395,17 @@ def run_ours(args):
         gather = RowGather(sizes, (dim,), dtype, device)
     gather_timer = [] if gather is not None else None
 
+    # A data loader knows its batch's lengths on the host: passing their sum
+    # lets the kernels launch blocks for the valid rows only.
+    valid_rows = None if (padlen is None or args.full_grid) else sum(lens)
+
     def step(lv, feats_, grad_, seq_or_cu, share_sms=False):
         for t in lv.values():
             t.grad = None
         if padlen is not None:
             out = ops.flash_spacetime_attention(lv["q"], lv["k"], lv["v"], feats_, lv["weight"],
-                                                lv["bias"], seq_or_cu, share_sms=share_sms)
+                                                lv["bias"], seq_or_cu, share_sms=share_sms,
+                                                valid_rows=valid_rows)
         else:
             out = ops.flash_spacetime_attention_varlen(lv["q"], lv["k"], lv["v"], feats_,
                                                        lv["weight"], lv["bias"], seq_or_cu,
@@ -523,6 +528,7 @@ def run_ours(args):
         "config": {"workload": args.workload, "events": n_events, "heads": heads,
                    "head_dim": dim, "channels": channels,
                    "padded_length": padlen, "coords": args.coords,
+                   "valid_rows_hint": valid_rows,
                    "valid_pairs_per_gpu": flops["pairs"],
                    "output_gather": (None if gather is None else
                                      f"all_gather_into_tensor of every rank's valid output rows, "
@@ -563,6 +569,9 @@ def main():
                          "(the default for config4, whose sharded run names it)")
     ap.add_argument("--no-gather", dest="gather_out", action="store_false",
                     help="multi-GPU: skip the all-gather of the outputs")
+    ap.add_argument("--full-grid", action="store_true",
+                    help="padded workloads: do not pass the valid row count (valid_rows), so "
+                         "the kernels launch blocks over all B x L rows")
     ap.add_argument("--coords", default="raw", choices=("raw", "scaled"))
     ap.add_argument("--seed", type=int, default=2026)
     ap.add_argument("--cpu-budget", type=float, default=12.0)

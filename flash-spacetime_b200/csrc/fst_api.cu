@@ -63,6 +63,7 @@ int check_problem(const FstProblem* p) {
     if ((int64_t)p->batch * p->max_len != p->total_rows)
       return fail(FST_ERR_INVALID, "padded total_rows must equal B*L");
   }
+  if (p->valid_rows < 0) return fail(FST_ERR_INVALID, "negative valid_rows");
   if (p->flags & ~FST_FLAG_SHARE_SMS)
     return fail(FST_ERR_INVALID, "unknown flags 0x%x", (unsigned)p->flags);
   if (p->qkv_row_stride) {

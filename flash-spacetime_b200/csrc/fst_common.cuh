@@ -45,6 +45,43 @@ __host__ __device__ __forceinline__ bool rows_interleaved(const FstProblem& p) {
   return p.packed != 0;
 }
 
+// Whether the 16-bit kernels take their CTAs' (event, block) pairs from the
+// device tile list (tile_prefix) rather than from a (L / BM, B) grid: always
+// in the packed layout, and in the padded ones when the caller gave the
+// valid row count (FstProblem::valid_rows) below B*L. The list then holds the
+// live blocks only and the kernels launch about valid_rows / BM + B CTAs.
+__host__ __device__ __forceinline__ bool uses_tile_list(const FstProblem& p) {
+  return is_varlen(p) ||
+         (p.valid_rows > 0 && p.valid_rows < p.total_rows && p.total_rows < (1ll << 31));
+}
+// A padded layout walked by the tile list: no CTA lies past an event's end,
+// so a few CTAs at the head of the grid write the zero padding rows
+// (pad_ctas), and the workspace holds a second prefix (of the padding row
+// counts) after the tile prefix.
+__host__ __device__ __forceinline__ bool list_padding(const FstProblem& p) {
+  return !is_varlen(p) && uses_tile_list(p);
+}
+// Upper bound on the rows the tile list covers.
+__host__ __device__ __forceinline__ int64_t list_rows(const FstProblem& p) {
+  return is_varlen(p) ? p.total_rows : p.valid_rows;
+}
+// CTAs that write the zero padding rows of a padded tile-list grid, for a
+// kernel that writes row_bytes per padding (row, head): one per 4 MiB of
+// padding (B*L minus the valid rows), at least 1 and at most 32. A CTA
+// stores at ~0.1 TB/s, so 32 of them leave most of the HBM bandwidth and
+// every other SM to the live blocks; the launch adds them to the grid.
+__host__ __device__ __forceinline__ int pad_ctas(const FstProblem& p, int row_bytes) {
+  if (!list_padding(p)) return 0;
+  const int64_t bytes = (p.total_rows - p.valid_rows) * p.heads * (int64_t)row_bytes;
+  const int64_t z = bytes >> 22;
+  return z < 1 ? 1 : (z > 32 ? 32 : (int)z);
+}
+// Ints of the tile-list workspace: the tile prefix [B + 1], then, for a
+// padded layout, the padding-row prefix [B + 1].
+__host__ __device__ __forceinline__ int64_t tile_list_ints(const FstProblem& p) {
+  return (int64_t)(p.batch + 1) * (list_padding(p) ? 2 : 1);
+}
+
 // Where one event lives. `row0` is the flat row of the event's first token in
 // the [rows] index space (padded: b*L, packed: cu[b]); `len` its valid length.
 // `base1`, `hs1` and `rs1` address its rows without any division: element

@@ -32,9 +32,10 @@ int make_head_map(CUtensorMap* map, const FstProblem& p, const void* base, int r
 bool fwd_supported(const FstProblem& p);
 size_t fwd_workspace(const FstProblem& p);
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
-// Exclusive prefix of ceil(len_b / bm) over the events of a packed batch, in
-// p.event_order when given, written to tile_start[0..B] (one small kernel; no
-// host synchronisation).
+// The device tile list (uses_tile_list): exclusive prefix of ceil(len_b / bm)
+// over the events, in p.event_order when given, written to tile_start[0..B],
+// and for a padded layout the prefix of the padding row counts after it (one
+// small kernel; no host synchronisation).
 void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st);
 int launch_bwd_rows(const FstBackwardArgs& a, cudaStream_t st, int* tile_start, void* u_ws,
                     void* wt_ws, void* qt_ws);

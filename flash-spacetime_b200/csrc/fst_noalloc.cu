@@ -13,7 +13,8 @@
 //
 // The array is kScratchBytes (256 KiB) per GPU. A problem whose workspace
 // (fst_forward_workspace_size) exceeds it -- a 16-bit batch of more than
-// 65535 events -- is rejected with FST_ERR_INVALID; problems that need no
+// 65535 events, or 32767 in a padded layout given valid_rows (whose tile list
+// holds two prefixes) -- is rejected with FST_ERR_INVALID; problems that need no
 // workspace (fp32 inputs) are not limited. Every GPU that loads the library
 // holds the array until the process exits.
 //
@@ -72,13 +73,14 @@ int scratch_for_current_device(void** out, char* err, size_t errlen) {
 extern "C" int fst_forward_noalloc(const FstForwardArgs* args, void* stream) {
   char err[256];
   if (!args) return fst::api_fail(FST_ERR_INVALID, "fst_forward_noalloc: null args");
-  // The tensor-core forward's workspace is the (batch + 1)-entry int32 tile
-  // prefix (fst::tc::fwd_workspace); the fp32 kernels need none.
+  // The tensor-core forward's workspace is the int32 tile-list prefixes
+  // (fst::tc::fwd_workspace); the fp32 kernels need none.
   const size_t need = fst_forward_workspace_size(&args->prob);
   if (need > kScratchBytes)
     return fst::api_fail(FST_ERR_INVALID,
                          "fst_forward_noalloc: %d events need %zu bytes of scratch, above the "
-                         "built-in scratch limit of %zu bytes (at most 65535 events; use "
+                         "built-in scratch limit of %zu bytes (at most 65535 events, 32767 padded with "
+                         "valid_rows; use "
                          "fst_forward with a caller workspace)",
                          args->prob.batch, need, kScratchBytes);
   void* scratch = nullptr;

@@ -105,26 +105,35 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   extern __shared__ __align__(128) unsigned char smem[];
   const FstProblem& p = a.prob;
 
+  const int h0 = blockIdx.z * heads_per_group;
+  const int NH = min(heads_per_group, p.heads - h0);
+  T* __restrict__ gdk = (T*)a.dk;
+  T* __restrict__ gdv = (T*)a.dv;
+
+  // Event and key block of this CTA: grid (L / BK, B, groups) over the
+  // padded layout, or entry blockIdx.x of the device tile list (the row
+  // kernel's, whose blocks are also BK rows).
   int b, kb;
-  if (!is_varlen(p)) {
+  if (uses_tile_list(p)) {
+    int t = blockIdx.x;
+    if (list_padding(p)) {
+      const int writers = pad_ctas(p, DH * 4);  // padding bytes per (row, head)
+      t = list_padded_role(p, tile_start, S::BK, writers, [&](int e, int r0, int r1, int nan) {
+        const EventSpan es = qkv_span(p, e, DH);
+        const uint32_t v2 = nan ? E::kNaN2 : 0u;
+        fill_rows<T, DH>(gdk, es, nullptr, nullptr, es, r0, r1, h0, NH, v2, 0.f);
+        fill_rows<T, DH>(gdv, es, nullptr, nullptr, es, r0, r1, h0, NH, v2, 0.f);
+      });
+      if (t < 0) return;
+    }
+    if (!list_tile(p, tile_start, t, b, kb)) return;
+  } else {
     b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
     kb = blockIdx.x;
-  } else {
-    const int t = blockIdx.x;
-    if (t >= tile_start[p.batch]) return;
-    int lo = 0, hi = p.batch - 1;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
-    }
-    kb = t - tile_start[lo];
-    b = p.event_order ? p.event_order[lo] : lo;
   }
   const EventSpan ev = event_span(p, b);
   const EventSpan evq = qkv_span(p, b, DH);  // k, v, dk, dv (a fused QKV buffer's row stride)
   const int k0 = kb * S::BK;
-  const int h0 = blockIdx.z * heads_per_group;
-  const int NH = min(heads_per_group, p.heads - h0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NE = S::NE;
   const int nthreads = blockDim.x;
@@ -132,8 +141,6 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   const T* __restrict__ gk = (const T*)a.k;
   const T* __restrict__ gv = (const T*)a.v;
   const T* __restrict__ gdo = (const T*)a.dout;
-  T* __restrict__ gdk = (T*)a.dk;
-  T* __restrict__ gdv = (T*)a.dv;
 
   if (k0 >= ev.len) {
     if (!is_varlen(p)) {
@@ -592,7 +599,7 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
   for (int rh = 0; rh < 2; ++rh) {
     const int j = r8 + 8 * rh;
     const bool valid = j < nvalid_k;
-    if (!valid && (is_varlen(p) || k0 + j >= p.max_len)) continue;
+    if (!valid && (uses_tile_list(p) || k0 + j >= p.max_len)) continue;
     const int64_t off = ev_off(evq, k0 + j, h, DH);
 #pragma unroll
     for (int nd = 0; nd < S::NTD; ++nd) {
@@ -656,9 +663,10 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
     const int per_group = (p.heads + groups - 1) / groups;
     const int threads = (per_group + S::NE) * 32;
     dim3 grid;
-    if (is_varlen(p)) {
+    if (uses_tile_list(p)) {
       // tile_start (16-row tiles) was built by the row kernel's launch.
-      const int64_t upper = (p.total_rows + S::BK - 1) / S::BK + p.batch;
+      const int64_t upper = (list_rows(p) + S::BK - 1) / S::BK + p.batch +
+          pad_ctas(p, DH * 4);
       grid = dim3((unsigned)upper, 1, groups);
     } else {
       grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
@@ -708,13 +716,13 @@ bool bwd_supported(const FstProblem& p) {
   return fwd_supported(p);  // same (Dh, C) list; every shape fits both kernels
 }
 
-// Workspace: [tile prefix, B+1 ints][u and w~, rows x H x C each
+// Workspace: [tile list prefixes, tile_list_ints][u and w~, rows x H x C each
 // in the 16-bit type, 256-byte aligned][qt = [q * scale], rows x H x Dh in
 // the 16-bit type] -- the row kernel writes the two projections there (when
 // the caller did not pass them) and the scaled q, the column kernel reads
 // them back.
 static size_t ws_proj_offset(const FstProblem& p) {
-  return ((size_t)(p.batch + 1) * sizeof(int) + 255) / 256 * 256;
+  return ((size_t)tile_list_ints(p) * sizeof(int) + 255) / 256 * 256;
 }
 static size_t ws_proj_bytes(const FstProblem& p) {
   return ((size_t)p.total_rows * p.heads * p.channels * 2 + 255) / 256 * 256;

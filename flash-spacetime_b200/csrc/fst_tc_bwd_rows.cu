@@ -138,38 +138,43 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   extern __shared__ __align__(1024) unsigned char smem[];
   const FstProblem& p = a.prob;
 
-  int b, qb;
-  if (!is_varlen(p)) {
-    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
-    qb = blockIdx.x;
-  } else {
-    const int t = blockIdx.x;
-    if (t >= tile_start[p.batch]) {
-      // Beyond the tile list: this CTA's dW partial slot still needs zeros.
-      const int64_t part = (int64_t)blockIdx.z * gridDim.x + blockIdx.x;
-      for (int i = threadIdx.x; i < DH * C; i += blockDim.x)
-        a.dw_partial[part * DH * C + i] = 0.f;
-      for (int i = threadIdx.x; i < DH; i += blockDim.x) a.db_partial[part * DH + i] = 0.f;
-      return;
-    }
-    int lo = 0, hi = p.batch - 1;
-    while (lo < hi) {
-      int mid = (lo + hi + 1) >> 1;
-      if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
-    }
-    qb = t - tile_start[lo];
-    b = p.event_order ? p.event_order[lo] : lo;
-  }
-  const int64_t part = is_varlen(p) ? ((int64_t)blockIdx.z * gridDim.x + blockIdx.x)
-                                : (((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x +
-                                   blockIdx.x);
+  const int h0 = blockIdx.z * heads_per_group;
+  const int NH = min(heads_per_group, p.heads - h0);
+  T* __restrict__ gdq = (T*)a.dq;
+  // This CTA's dW / db partial slot: one per CTA of the grid.
+  const int64_t part = ((int64_t)blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
   float* dwp = a.dw_partial + part * DH * C;
   float* dbp = a.db_partial + part * DH;
+
+  // Event and row block of this CTA: grid (L / BM, B, groups) over the
+  // padded layout, or entry blockIdx.x of the device tile list.
+  int b, qb;
+  if (uses_tile_list(p)) {
+    int t = blockIdx.x;
+    if (list_padding(p)) {
+      const int writers = pad_ctas(p, DH * 2 + 8);  // padding bytes per (row, head)
+      t = list_padded_role(p, tile_start, S::BM, writers, [&](int e, int r0, int r1, int nan) {
+        const EventSpan es = event_span(p, e);
+        fill_rows<T, DH>(gdq, qkv_span(p, e, DH), a.delta, a.sigma, es, r0, r1, h0, NH,
+                         nan ? E::kNaN2 : 0u, nan ? __int_as_float(0x7fc00000) : 0.f);
+      });
+    }
+    const bool poisoned = t == kRolePoisoned;
+    if (t < 0 || !list_tile(p, tile_start, t, b, qb)) {
+      // No block to compute: the partial slot holds zeros (NaN when the
+      // caller's valid_rows was too small).
+      const float v = poisoned ? __int_as_float(0x7fc00000) : 0.f;
+      for (int i = threadIdx.x; i < DH * C; i += blockDim.x) dwp[i] = v;
+      for (int i = threadIdx.x; i < DH; i += blockDim.x) dbp[i] = v;
+      return;
+    }
+  } else {
+    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
+    qb = blockIdx.x;
+  }
   const EventSpan ev = event_span(p, b);
   const EventSpan evq = qkv_span(p, b, DH);  // q, k, v, dq (a fused QKV buffer's row stride)
   const int q0 = qb * S::BM;
-  const int h0 = blockIdx.z * heads_per_group;
-  const int NH = min(heads_per_group, p.heads - h0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NE = S::NE;
   const int nthreads = blockDim.x;
@@ -179,7 +184,6 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
   const T* __restrict__ gv = (const T*)a.v;
   const T* __restrict__ gdo = (const T*)a.dout;
   const T* __restrict__ gout = (const T*)a.out;
-  T* __restrict__ gdq = (T*)a.dq;
 
   if (q0 >= ev.len) {
     for (int i = threadIdx.x; i < DH * C; i += nthreads) dwp[i] = 0.f;
@@ -974,7 +978,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     for (int rh = 0; rh < 2; ++rh) {
       const int q = r8 + 8 * rh;
       const bool valid = q < nvalid_q;
-      if (!valid && (is_varlen(p) || q0 + q >= p.max_len)) continue;
+      if (!valid && (uses_tile_list(p) || q0 + q >= p.max_len)) continue;
       T* orow = gdq + ev_off(evq, q0 + q, h, DH);
 #pragma unroll
       for (int nd = 0; nd < S::NTD; ++nd) {
@@ -1102,8 +1106,9 @@ template <int DH, int C>
 static dim3 rows_grid(const FstProblem& p) {
   using S = RowShape<DH, C>;
   const int groups = (p.heads + S::HP - 1) / S::HP;
-  if (is_varlen(p)) {
-    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
+  if (uses_tile_list(p)) {
+    const int64_t upper = (list_rows(p) + S::BM - 1) / S::BM + p.batch +
+        pad_ctas(p, DH * 2 + 8);
     return dim3((unsigned)upper, 1, groups);
   }
   return dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
@@ -1131,7 +1136,7 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   const int groups = (int)grid.z;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;
-  if (is_varlen(p)) tile_prefix(p, S::BM, tile_start, st);
+  if (uses_tile_list(p)) tile_prefix(p, S::BM, tile_start, st);
   if (grid.x == 0 || grid.y == 0) return FST_OK;
   bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
       a, tile_start, per_group, (T*)u_ws, (T*)wt_ws, (T*)qt_ws, maps);

@@ -28,6 +28,7 @@ struct __align__(64) TmaPair {
 template <typename T> struct Elem;
 template <> struct Elem<__nv_bfloat16> {
   static constexpr uint32_t kOnes = 0x3f803f80u;  // (1.0, 1.0)
+  static constexpr uint32_t kNaN2 = 0x7fc07fc0u;  // (NaN, NaN)
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -38,6 +39,7 @@ template <> struct Elem<__nv_bfloat16> {
 };
 template <> struct Elem<__half> {
   static constexpr uint32_t kOnes = 0x3c003c00u;  // (1.0, 1.0)
+  static constexpr uint32_t kNaN2 = 0x7e007e00u;  // (NaN, NaN)
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     uint32_t r;
     asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
@@ -377,6 +379,113 @@ __device__ __forceinline__ void stage_rows(const T* __restrict__ src, const Even
       v = *(const uint4*)(src + ev_off(ev, i0 + q, h0 + h, C) + c * 8);
     *(uint4*)(tile + swz<RBC>(q * 16 + h, c)) = v;
   }
+}
+
+// ---- the device tile list ---------------------------------------------------
+
+// Entry t of the tile list (tile_prefix: the exclusive prefix tile_start[0..B]
+// of each event's block count, events in p.event_order): its event b and the
+// block's index within the event. False past the list's end.
+__device__ __forceinline__ bool list_tile(const FstProblem& p, const int* __restrict__ tile_start,
+                                          int t, int& b, int& blk) {
+  if (t >= tile_start[p.batch]) return false;
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {  // last position with tile_start[pos] <= t
+    const int mid = (lo + hi + 1) >> 1;
+    if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
+  }
+  blk = t - tile_start[lo];
+  b = p.event_order ? p.event_order[lo] : lo;
+  return true;
+}
+
+// Writes the 16-bit pair `v2` to rows [r0, r1) of heads [h0, h0 + nh) of event
+// e in a [*, H, DIM]-addressed tensor (16-byte stores; DIM a multiple of 8),
+// and `s` to the same (row, head) entries of the fp32 vectors s0 and s1 (each
+// may be NULL) addressed by es.
+template <typename T, int DIM>
+__device__ __forceinline__ void fill_rows(T* __restrict__ base, const EventSpan& e,
+                                          float* __restrict__ s0, float* __restrict__ s1,
+                                          const EventSpan& es, int r0, int r1, int h0, int nh,
+                                          uint32_t v2, float s) {
+  constexpr int CH = DIM / 8;
+  const int per_row = nh * CH;
+  const int n = (r1 - r0) * per_row;
+  for (int idx = threadIdx.x; idx < n; idx += blockDim.x) {
+    const int r = idx / per_row, rem = idx - r * per_row;
+    const int h = h0 + rem / CH, c = rem % CH;
+    // Streaming stores: nothing reads these rows again in the kernel, so they
+    // should not push the live blocks' K / V out of L2.
+    __stcs((uint4*)(base + ev_off(e, r0 + r, h, DIM) + c * 8), make_uint4(v2, v2, v2, v2));
+    if (c == 0) {
+      if (s0) __stcs(s0 + ev_off(es, r0 + r, h, 1), s);
+      if (s1) __stcs(s1 + ev_off(es, r0 + r, h, 1), s);
+    }
+  }
+}
+
+// A padded layout walked by the tile list has no CTA past an event's end, so
+// the padding rows [len_b, max_len) of all events are split evenly over the
+// first n CTAs of the list (pad_start: the exclusive prefix of max_len - len_b
+// in natural event order, written by tile_prefix). CTA t calls fn(b, r0, r1)
+// for each row range of its share -- one or a few, in ascending rows.
+template <typename F>
+__device__ __forceinline__ void padding_share(const FstProblem& p,
+                                              const int* __restrict__ pad_start, int t, int n,
+                                              F&& fn) {
+  const int64_t total = pad_start[p.batch];
+  int64_t r = total * t / n;
+  const int64_t r1 = total * (t + 1) / n;
+  if (r >= r1) return;
+  int lo = 0, hi = p.batch - 1;
+  while (lo < hi) {  // the event whose padding holds row r
+    const int mid = (lo + hi + 1) >> 1;
+    if (pad_start[mid] <= r) lo = mid; else hi = mid - 1;
+  }
+  for (int b = lo; b < p.batch && r < r1; ++b) {
+    const int64_t s0 = pad_start[b];
+    const int64_t s1 = min(r1, (int64_t)pad_start[b + 1]);
+    if (s1 <= r) continue;                                 // no padding rows in event b
+    const int len = p.max_len - (pad_start[b + 1] - pad_start[b]);  // clamped seqlens[b]
+    fn(b, len + (int)(r - s0), len + (int)(s1 - s0));
+    r = s1;
+  }
+}
+
+// Role of a CTA in a padded layout walked by the tile list (list_padding).
+// Such a grid is n_tiles live blocks after zc = gridDim.x - n_tiles CTAs.
+// The first nz = min(zc, writers) of those write the zero padding rows,
+// split evenly between them, while the live blocks run beside them
+// (`writers` = pad_ctas, which the launch adds to the grid); the others exit.
+// Returns the tile-list entry this CTA computes, or kRoleDone. When the
+// caller's valid_rows was too small for the grid to hold every live block
+// (zc < 1), every CTA writes its share of the padding and NaN in every valid
+// row of the blocks t, t + g, ..., and returns kRolePoisoned. fill(b, r0, r1,
+// nan) writes rows [r0, r1) of event b: zeros, or NaN when nan != 0.
+constexpr int kRoleDone = -1, kRolePoisoned = -2;
+template <typename F>
+__device__ __forceinline__ int list_padded_role(const FstProblem& p,
+                                                const int* __restrict__ tile_start, int bm,
+                                                int writers, F&& fill) {
+  const int n_tiles = tile_start[p.batch];
+  const int g = gridDim.x, t = blockIdx.x;
+  const int zc = g - n_tiles;
+  const int* pad_start = tile_start + p.batch + 1;
+  auto zero = [&](int b, int r0, int r1) { fill(b, r0, r1, 0); };
+  if (zc >= 1) {
+    if (t >= zc) return t - zc;
+    const int nz = min(zc, writers);
+    if (t < nz) padding_share(p, pad_start, t, nz, zero);
+    return kRoleDone;
+  }
+  padding_share(p, pad_start, t, g, zero);
+  for (int tt = t; tt < n_tiles; tt += g) {
+    int b, blk;
+    list_tile(p, tile_start, tt, b, blk);
+    const int len = min(max(p.seqlens[b], 0), p.max_len);
+    fill(b, blk * bm, min(len, (blk + 1) * bm), 1);
+  }
+  return kRolePoisoned;
 }
 
 }  // namespace tc

@@ -139,28 +139,6 @@ __device__ __forceinline__ int bar_bias_empty(int s) { return 3 + s; }
 __device__ __forceinline__ int bar_p_full(int s) { return 5 + s; }
 __device__ __forceinline__ int bar_p_empty(int s) { return 7 + s; }
 
-// Event and query block of this CTA. Padded layout: grid (L/BM, B, groups).
-// Packed layout: blockIdx.x indexes the flattened list of (event, block)
-// tiles whose exclusive prefix is tile_start[0..B].
-__device__ __forceinline__ bool fwd_tile(const FstProblem& p, const int* tile_start, int& b,
-                                         int& qb) {
-  if (!is_varlen(p)) {
-    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
-    qb = blockIdx.x;
-    return true;
-  }
-  const int t = blockIdx.x;
-  if (t >= tile_start[p.batch]) return false;
-  int lo = 0, hi = p.batch - 1;
-  while (lo < hi) {  // last b with tile_start[b] <= t
-    int mid = (lo + hi + 1) >> 1;
-    if (tile_start[mid] <= t) lo = mid; else hi = mid - 1;
-  }
-  qb = t - tile_start[lo];
-  b = p.event_order ? p.event_order[lo] : lo;
-  return true;
-}
-
 template <typename T, int DH, int C>
 __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     fwd_tc_kernel(const FstForwardArgs a, const int* __restrict__ tile_start, int heads_per_group,
@@ -170,16 +148,35 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   extern __shared__ __align__(1024) unsigned char smem[];
   const FstProblem& p = a.prob;
 
-  int b, qb;
-  if (!fwd_tile(p, tile_start, b, qb)) return;
-  const EventSpan ev = event_span(p, b);
-  const EventSpan evq = qkv_span(p, b, DH);  // q, k, v (a fused QKV buffer's row stride)
-  const int q0 = qb * S::BM;
   // Heads are split into gridDim.z groups of heads_per_group (<= HP); the
   // block is sized for heads_per_group head warps, so in a shorter last group
   // the surplus warps idle (they only join the CTA-wide barriers).
   const int h0 = blockIdx.z * heads_per_group;
   const int NH = min(heads_per_group, p.heads - h0);
+  T* __restrict__ gout = (T*)a.out;
+
+  // Event and query block of this CTA: grid (L / BM, B, groups) over the
+  // padded layout, or entry blockIdx.x of the device tile list.
+  int b, qb;
+  if (uses_tile_list(p)) {
+    int t = blockIdx.x;
+    if (list_padding(p)) {
+      const int writers = pad_ctas(p, DH * 2 + 4);  // padding bytes per (row, head)
+      t = list_padded_role(p, tile_start, S::BM, writers, [&](int e, int r0, int r1, int nan) {
+        const EventSpan es = event_span(p, e);
+        fill_rows<T, DH>(gout, es, a.lse, nullptr, es, r0, r1, h0, NH, nan ? E::kNaN2 : 0u,
+                         nan ? __int_as_float(0x7fc00000) : 0.f);
+      });
+      if (t < 0) return;
+    }
+    if (!list_tile(p, tile_start, t, b, qb)) return;
+  } else {
+    b = p.event_order ? p.event_order[blockIdx.y] : (int)blockIdx.y;
+    qb = blockIdx.x;
+  }
+  const EventSpan ev = event_span(p, b);
+  const EventSpan evq = qkv_span(p, b, DH);  // q, k, v (a fused QKV buffer's row stride)
+  const int q0 = qb * S::BM;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int NE = S::NE;
   const int nthreads = blockDim.x;
@@ -187,7 +184,6 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
   const T* __restrict__ gk = (const T*)a.k;
   const T* __restrict__ gv = (const T*)a.v;
   const T* __restrict__ gu = (const T*)a.u;
-  T* __restrict__ gout = (T*)a.out;
   const bool attn = p.use_attn_bias != 0;
   const bool act = p.use_act_bias != 0;
 
@@ -855,7 +851,7 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
       for (int rh = 0; rh < 2; ++rh) {
         const int q = rg * 16 + r8 + 8 * rh;
         const bool valid = q < nvalid_q;
-        if (!valid && (is_varlen(p) || q0 + q >= p.max_len)) continue;
+        if (!valid && (uses_tile_list(p) || q0 + q >= p.max_len)) continue;
         const float il = valid ? 1.f / lrun[rg][rh] : 0.f;
         T* orow = gout + ev_off(ev, q0 + q, h, DH);
 #pragma unroll
@@ -885,49 +881,77 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 
 // ---------------------------------------------------------------------------
 
-__global__ void tile_prefix_kernel(const int32_t* __restrict__ cu,
-                                   const int32_t* __restrict__ order, int batch, int bm,
-                                   int* __restrict__ tile_start) {
-  // Single-CTA exclusive scan of ceil(len_b / bm) over the events, taken in
-  // the given order (position k holds event order[k]) or the natural one.
-  __shared__ int warp_sums[32];
-  __shared__ int carry;
-  if (threadIdx.x == 0) carry = 0;
+__global__ void tile_prefix_kernel(const FstProblem p, int bm, int* __restrict__ tile_start) {
+  // Single-CTA exclusive scans over the events: of ceil(len_b / bm), the
+  // events taken in p.event_order (position k holds event order[k]) or the
+  // natural one, into tile_start[0..B]; for a padded layout walked by the
+  // tile list, also of the padding row counts max_len - len_b in natural
+  // order, into tile_start[B+1 .. 2B+1].
+  __shared__ int2 warp_sums[32];
+  __shared__ int2 carry;
+  const bool pad = list_padding(p);
+  const int batch = p.batch;
+  if (threadIdx.x == 0) carry = make_int2(0, 0);
   __syncthreads();
   for (int base = 0; base < batch; base += blockDim.x) {
-    const int b = base + threadIdx.x;
-    const int ev = b < batch ? (order ? order[b] : b) : 0;
-    const int v = b < batch ? (cu[ev + 1] - cu[ev] + bm - 1) / bm : 0;
-    int x = v;
+    const int k = base + threadIdx.x;
+    int2 v = make_int2(0, 0);
+    if (k < batch) {
+      const int ev = p.event_order ? p.event_order[k] : k;
+      int len;
+      if (is_varlen(p)) {
+        len = p.cu_seqlens[ev + 1] - p.cu_seqlens[ev];
+      } else {
+        len = min(max(p.seqlens[ev], 0), p.max_len);
+      }
+      v.x = (len + bm - 1) / bm;
+      if (pad) v.y = p.max_len - min(max(p.seqlens[k], 0), p.max_len);
+    }
+    int2 x = v;
     const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
-      const int y = __shfl_up_sync(0xffffffffu, x, o);
-      if (lane >= o) x += y;
+      const int yx = __shfl_up_sync(0xffffffffu, x.x, o);
+      const int yy = __shfl_up_sync(0xffffffffu, x.y, o);
+      if (lane >= o) {
+        x.x += yx;
+        x.y += yy;
+      }
     }
     if (lane == 31) warp_sums[w] = x;
     __syncthreads();
     if (w == 0) {
-      int ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : 0;
+      int2 ws = lane < (int)(blockDim.x >> 5) ? warp_sums[lane] : make_int2(0, 0);
 #pragma unroll
       for (int o = 1; o < 32; o <<= 1) {
-        const int y = __shfl_up_sync(0xffffffffu, ws, o);
-        if (lane >= o) ws += y;
+        const int yx = __shfl_up_sync(0xffffffffu, ws.x, o);
+        const int yy = __shfl_up_sync(0xffffffffu, ws.y, o);
+        if (lane >= o) {
+          ws.x += yx;
+          ws.y += yy;
+        }
       }
       warp_sums[lane] = ws;
     }
     __syncthreads();
-    const int incl = x + (w > 0 ? warp_sums[w - 1] : 0) + carry;
-    if (b < batch) tile_start[b] = incl - v;
+    const int2 before = w > 0 ? warp_sums[w - 1] : make_int2(0, 0);
+    const int2 incl = make_int2(x.x + before.x + carry.x, x.y + before.y + carry.y);
+    if (k < batch) {
+      tile_start[k] = incl.x - v.x;
+      if (pad) tile_start[batch + 1 + k] = incl.y - v.y;
+    }
     __syncthreads();
     if (threadIdx.x == blockDim.x - 1) carry = incl;
     __syncthreads();
   }
-  if (threadIdx.x == 0) tile_start[batch] = carry;
+  if (threadIdx.x == 0) {
+    tile_start[batch] = carry.x;
+    if (pad) tile_start[2 * batch + 1] = carry.y;
+  }
 }
 
 void tile_prefix(const FstProblem& p, int bm, int* tile_start, cudaStream_t st) {
-  tile_prefix_kernel<<<1, 1024, 0, st>>>(p.cu_seqlens, p.event_order, p.batch, bm, tile_start);
+  tile_prefix_kernel<<<1, 1024, 0, st>>>(p, bm, tile_start);
   count_launch();
 }
 
@@ -949,9 +973,10 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
   const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
   const int threads = (per_group + S::NE) * 32;
   dim3 grid;
-  if (is_varlen(p)) {
+  if (uses_tile_list(p)) {
     tile_prefix(p, S::BM, tile_start, st);
-    const int64_t upper = (p.total_rows + S::BM - 1) / S::BM + p.batch;
+    const int64_t upper = (list_rows(p) + S::BM - 1) / S::BM + p.batch +
+        pad_ctas(p, DH * 2 + 4);
     grid = dim3((unsigned)upper, 1, groups);
   } else {
     grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
@@ -985,9 +1010,9 @@ bool fwd_supported(const FstProblem& p) {
          (D == 16 && C == 16) || (D == 48 && C == 48);
 }
 
-// Workspace: the packed layout's per-event tile prefix, B+1 ints.
+// Workspace: the tile list's prefixes (tile_list_ints).
 size_t fwd_workspace(const FstProblem& p) {
-  return ((size_t)(p.batch + 1) * sizeof(int) + 15) / 16 * 16;
+  return ((size_t)tile_list_ints(p) * sizeof(int) + 15) / 16 * 16;
 }
 
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st) {

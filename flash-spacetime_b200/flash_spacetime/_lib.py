@@ -21,7 +21,7 @@ FST_ERR_CUDA = 3
 FST_ERR_WORKSPACE = 4
 FST_ERR_DEVICE = 5
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 FST_FLAG_SHARE_SMS = 1  # FstProblem.flags: another kernel shares the SMs
 
 EXPORTED = (
@@ -61,6 +61,7 @@ class FstProblem(ctypes.Structure):
         ("event_order", ctypes.c_void_p),
         ("qkv_row_stride", ctypes.c_int32),
         ("flags", ctypes.c_int32),
+        ("valid_rows", ctypes.c_int64),
     ]
 
 

@@ -102,19 +102,50 @@ def seqlens_from_mask(mask: Tensor, validate: bool = True) -> Tensor:
     mask whose valid tokens are not a prefix raises ValueError (this check
     reads one flag back from the device).
     """
+    return _mask_lengths(mask, validate)[0]
+
+
+def _mask_lengths(mask: Tensor, validate: bool) -> Tuple[Tensor, int]:
+    """(seqlens_from_mask, the valid row count when the check read it back
+    with its flag -- one device-to-host read for both -- else 0)."""
     if mask.dim() != 2:
         raise ValueError(f"key_padding_mask must be [B, L], got {tuple(mask.shape)}")
     pad = mask if mask.dtype == torch.bool else torch.isneginf(mask)
     valid = ~pad
     lengths = valid.sum(1, dtype=torch.int32)
-    if validate:
-        pos = torch.arange(mask.shape[1], device=mask.device)
-        if not torch.equal(valid, pos[None, :] < lengths[:, None]):
-            raise ValueError(
-                "key_padding_mask must mark a prefix of each event as valid "
-                "(front-packed padding); reorder the tokens of each event"
-            )
-    return lengths
+    if not validate:
+        return lengths, 0
+    pos = torch.arange(mask.shape[1], device=mask.device)
+    prefix = (valid == (pos[None, :] < lengths[:, None])).all()
+    ok, total = torch.stack([prefix.to(torch.int64), lengths.sum(dtype=torch.int64)]).tolist()
+    if not ok:
+        raise ValueError(
+            "key_padding_mask must mark a prefix of each event as valid "
+            "(front-packed padding); reorder the tokens of each event"
+        )
+    return lengths, int(total)
+
+
+def _padded_lengths(seqlens: Any, mask: Optional[Tensor], batch: int, length: int,
+                    device: torch.device, validate: bool,
+                    valid_rows: Optional[int]) -> Tuple[Tensor, int]:
+    """Lengths of a padded batch from ``seqlens`` (``[B]``, on any device, or a
+    ``[B, L]`` mask) or ``key_padding_mask``, and the valid row count as far
+    as the host knows it (0 = unknown)."""
+    hint = 0
+    if mask is not None:
+        if seqlens is not None:
+            raise ValueError("pass seqlens or key_padding_mask, not both")
+        seqlens, hint = _mask_lengths(mask, validate)
+    elif seqlens is None:
+        seqlens = torch.full((batch,), length, dtype=torch.int32, device=device)
+    elif isinstance(seqlens, Tensor) and seqlens.dim() == 2:
+        seqlens, hint = _mask_lengths(seqlens, validate)
+    if valid_rows is not None:
+        if int(valid_rows) < 0:
+            raise ValueError(f"valid_rows must be >= 0, got {valid_rows}")
+        hint = int(valid_rows)
+    return seqlens, hint
 
 
 class _Problem:
@@ -135,8 +166,10 @@ class _Problem:
         host_projection: bool = False,
         qkv_row_stride: int = 0,
         share_sms: bool = False,
+        valid_rows: int = 0,
     ) -> None:
         self.packed = cu_seqlens is not None
+        self.valid_rows = 0
         self.share_sms = bool(share_sms)
         self.host_projection = bool(host_projection)
         self.qkv_row_stride = int(qkv_row_stride)
@@ -170,9 +203,22 @@ class _Problem:
             else:
                 batch, heads, length, dim = q.shape
             self.cu = None
-            self.seq = seqlens.to(device=q.device, dtype=torch.int32).contiguous()
+            # Lengths held on the host (a list or a CPU tensor, as a data
+            # loader has them) also give the valid row count, with which the
+            # kernels launch blocks for the valid rows only.
+            host = None
+            if not (isinstance(seqlens, Tensor) and seqlens.is_cuda):
+                host = torch.as_tensor(seqlens, dtype=torch.int64, device="cpu")
+            self.seq = torch.as_tensor(seqlens).to(device=q.device, dtype=torch.int32).contiguous()
             if self.seq.shape != (batch,):
                 raise ValueError(f"seqlens must be [B] = [{batch}], got {tuple(self.seq.shape)}")
+            if host is not None:
+                known = int(host.clamp(0, length).sum())
+                if valid_rows and valid_rows < known:
+                    raise ValueError(f"valid_rows (={valid_rows}) is below the sum of the "
+                                     f"lengths (={known})")
+                valid_rows = valid_rows or known
+            self.valid_rows = int(valid_rows)
             rows = batch * length
             # Longest events first: their row / key blocks are scheduled
             # before the short ones', which balances the SMs (the results
@@ -235,6 +281,7 @@ class _Problem:
         p.event_order = _ptr(self.order)
         p.qkv_row_stride = self.qkv_row_stride
         p.flags = _lib.FST_FLAG_SHARE_SMS if self.share_sms else 0
+        p.valid_rows = self.valid_rows
         return p
 
     def stat_shape(self) -> Tuple[int, ...]:
@@ -371,6 +418,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
         layout: str = "bhld",
         host_projection: bool = False,
         share_sms: bool = False,
+        valid_rows: int = 0,
     ) -> Tensor:
         if feats.requires_grad:
             raise ValueError("feats (detector data) must not require grad")
@@ -380,7 +428,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             raise ValueError("q, k and v must have the same dtype")
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale,
                       use_attn_bias, use_activation_bias, layout, host_projection,
-                      share_sms=share_sms)
+                      share_sms=share_sms, valid_rows=valid_rows)
         qc, kc, vc = (_dense(t) for t in (q, k, v))
         out, lse = fused_forward(pb, qc, kc, vc)
         ctx.save_for_backward(qc, kc, vc, out, lse)
@@ -404,7 +452,7 @@ class _FlashSpacetimeAttention(torch.autograd.Function):
             g["dq"] if need[0] else None,
             g["dk"] if need[1] else None,
             g["dv"] if need[2] else None,
-            None, dw, db, None, None, None, None, None, None, None, None,
+            None, dw, db, None, None, None, None, None, None, None, None, None,
         )
 
 
@@ -425,6 +473,7 @@ def flash_spacetime_attention(
     validate_mask: bool = True,
     host_projection: bool = False,
     share_sms: bool = False,
+    valid_rows: Optional[int] = None,
 ) -> Tensor:
     """Fused spacetime-bias attention on a padded batch (upstream forward.py:481-501).
 
@@ -450,19 +499,22 @@ def flash_spacetime_attention(
     kernel beside the op on every SM (a data loader's host-to-device copy of
     the next batch on a side stream, ``upload_valid_rows``): the backward
     then leaves room on each SM for it. Results do not depend on it.
+
+    ``valid_rows`` is the number of valid rows, the sum of the lengths (or
+    any larger number), when the caller knows it on the host -- a data loader
+    does. The kernels then launch blocks for the valid rows only, not for
+    ``B * L``; most of a padded batch of short events is padding. Lengths
+    passed on the host (a list or a CPU tensor as the 7th argument) and a
+    validated mask give it without the argument. Results do not depend on
+    it, except that a number below the true sum turns every valid output
+    row (and gradient row) into NaN.
     """
     length = q.shape[1] if layout == "blhd" else q.shape[2]
-    if key_padding_mask is not None:
-        if seqlens is not None:
-            raise ValueError("pass seqlens or key_padding_mask, not both")
-        seqlens = seqlens_from_mask(key_padding_mask, validate_mask)
-    elif seqlens is None:
-        seqlens = torch.full((q.shape[0],), length, dtype=torch.int32, device=q.device)
-    elif seqlens.dim() == 2:
-        seqlens = seqlens_from_mask(seqlens, validate_mask)
+    seqlens, hint = _padded_lengths(seqlens, key_padding_mask, q.shape[0], length, q.device,
+                                    validate_mask, valid_rows)
     return _FlashSpacetimeAttention.apply(
         q, k, v, feats, weight, bias, seqlens, None,
-        scale, use_attn_bias, use_activation_bias, layout, host_projection, share_sms,
+        scale, use_attn_bias, use_activation_bias, layout, host_projection, share_sms, hint,
     )
 
 
@@ -512,6 +564,7 @@ class _FlashSpacetimeQKV(torch.autograd.Function):
         use_attn_bias: bool,
         use_activation_bias: bool,
         host_projection: bool,
+        valid_rows: int = 0,
     ) -> Tensor:
         if feats.requires_grad:
             raise ValueError("feats (detector data) must not require grad")
@@ -519,7 +572,8 @@ class _FlashSpacetimeQKV(torch.autograd.Function):
         q, k, v = qkv.select(-3, 0), qkv.select(-3, 1), qkv.select(-3, 2)
         heads, dim = q.shape[-2], q.shape[-1]
         pb = _Problem(q, feats, weight, bias, seqlens, cu_seqlens, scale, use_attn_bias,
-                      use_activation_bias, "blhd", host_projection, 3 * heads * dim)
+                      use_activation_bias, "blhd", host_projection, 3 * heads * dim,
+                      valid_rows=valid_rows)
         out, lse = fused_forward(pb, q, k, v)
         ctx.save_for_backward(qkv, out, lse)
         ctx.pb = pb
@@ -540,7 +594,8 @@ class _FlashSpacetimeQKV(torch.autograd.Function):
         db = None
         if ctx.bias_dtype is not None and proj_used and need[3]:
             db = g["db"].to(ctx.bias_dtype)
-        return (dqkv if need[0] else None, None, dw, db, None, None, None, None, None, None)
+        return (dqkv if need[0] else None, None, dw, db, None, None, None, None, None, None,
+                None)
 
 
 def flash_spacetime_attention_qkv(
@@ -557,6 +612,7 @@ def flash_spacetime_attention_qkv(
     key_padding_mask: Optional[Tensor] = None,
     validate_mask: bool = True,
     host_projection: bool = False,
+    valid_rows: Optional[int] = None,
 ) -> Tensor:
     """The op on a fused QKV projection, read in place (no head split).
 
@@ -568,24 +624,19 @@ def flash_spacetime_attention_qkv(
     each row's q, k and v where the projection wrote them, and the gradient
     comes back as one ``[.., 3, H, Dh]`` tensor. Returns ``[B, L, H, Dh]``
     (or ``[T, H, Dh]``) in qkv's dtype with padding rows exactly 0.
+    ``valid_rows`` (padded only) as for :func:`flash_spacetime_attention`.
     """
     if qkv.dim() not in (4, 5) or qkv.shape[-3] != 3:
         raise ValueError(f"qkv must be [B, L, 3, H, Dh] or [T, 3, H, Dh], got {tuple(qkv.shape)}")
     packed = cu_seqlens is not None
     if packed != (qkv.dim() == 4):
         raise ValueError("a [T, 3, H, Dh] qkv needs cu_seqlens; a [B, L, 3, H, Dh] one does not")
+    hint = 0
     if not packed:
-        if key_padding_mask is not None:
-            if seqlens is not None:
-                raise ValueError("pass seqlens or key_padding_mask, not both")
-            seqlens = seqlens_from_mask(key_padding_mask, validate_mask)
-        elif seqlens is None:
-            seqlens = torch.full((qkv.shape[0],), qkv.shape[1], dtype=torch.int32,
-                                 device=qkv.device)
-        elif seqlens.dim() == 2:
-            seqlens = seqlens_from_mask(seqlens, validate_mask)
+        seqlens, hint = _padded_lengths(seqlens, key_padding_mask, qkv.shape[0], qkv.shape[1],
+                                        qkv.device, validate_mask, valid_rows)
     return _FlashSpacetimeQKV.apply(qkv, feats, weight, bias, seqlens, cu_seqlens, scale,
-                                    use_attn_bias, use_activation_bias, host_projection)
+                                    use_attn_bias, use_activation_bias, host_projection, hint)
 
 
 def flash_spacetime_attention_nested(

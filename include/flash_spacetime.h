@@ -50,7 +50,7 @@
 extern "C" {
 #endif
 
-#define FST_ABI_VERSION 4
+#define FST_ABI_VERSION 5
 
 /* Storage dtype of q, k, v, u, wt, out, dout, dq, dk, dv. */
 enum FstDtype { FST_F32 = 0, FST_BF16 = 1, FST_F16 = 2 };
@@ -107,6 +107,17 @@ typedef struct FstProblem {
   int32_t qkv_row_stride;
   /* FST_FLAG_* bits (performance hints; results do not depend on them). */
   int32_t flags;
+  /* Padded layouts (packed 0 or 2): sum over events of min(seqlens[b],
+   * max_len) -- the valid rows -- or any larger value, when the caller knows
+   * it on the host (a data loader does); 0 = unknown. With it the 16-bit
+   * kernels launch blocks for about that many rows, taken from a device tile
+   * list as in the packed layout, instead of max_len rows per event, and the
+   * live blocks write the zero padding rows between them. A value below the
+   * true sum is detected on the device: every valid row of every output is
+   * then NaN (padding rows stay 0). Ignored for packed == 1 and when >=
+   * total_rows. No upstream counterpart (its grid is (L / BM, B),
+   * forward.py:253-255). */
+  int64_t valid_rows;
 } FstProblem;
 
 /* Another kernel runs beside this call on every SM -- typically the host to
@@ -179,7 +190,8 @@ int fst_backward(const FstBackwardArgs* args, void* stream);
  * workspace. This variant ignores args->workspace and takes that scratch from
  * a 256 KiB array built into the library (one per GPU, held until the process
  * exits); it allocates nothing. A problem whose fst_forward_workspace_size
- * exceeds 256 KiB (16-bit inputs with more than 65535 events) is rejected
+ * exceeds 256 KiB (16-bit inputs with more than 65535 events, or 32767 in a
+ * padded layout given valid_rows) is rejected
  * with FST_ERR_INVALID. The first call on a device looks up the array's
  * address and keeps it for the life of the process (make that call before any
  * stream capture; after a cudaDeviceReset of that device the entry point must

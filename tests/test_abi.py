@@ -137,3 +137,45 @@ def test_upload_valid_rows_checks_arguments():
     src = torch.zeros(2, 3, 8, 4)
     with pytest.raises(ValueError, match="CPU tensor"):
         ops.upload_valid_rows(src.clone(), src, [1, 2])
+
+
+def test_valid_rows_is_checked_and_sizes_the_workspace():
+    # A negative valid_rows is refused before any launch. A padded problem
+    # given valid_rows below B*L walks the device tile list: its workspace
+    # holds the tile prefix and the padding-row prefix (2 * (B + 1) ints).
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.packed, p.batch, p.heads, p.max_len = 1, 0, 100, 12, 64
+    p.head_dim, p.channels, p.feat_stride, p.total_rows = 32, 16, 4, 6400
+    p.seqlens = p.feats = p.freqs = 256  # never dereferenced by these calls
+    full = lib.fst_forward_workspace_size(ctypes.byref(p))
+    p.valid_rows = 1000
+    listed = lib.fst_forward_workspace_size(ctypes.byref(p))
+    assert full == (101 * 4 + 15) // 16 * 16
+    assert listed == (2 * 101 * 4 + 15) // 16 * 16
+    p.valid_rows = 6400  # not below B*L: the full grid, no list
+    assert lib.fst_forward_workspace_size(ctypes.byref(p)) == full
+    p.valid_rows = -1
+    a = _lib.FstForwardArgs()
+    a.prob = p
+    assert lib.fst_forward(ctypes.byref(a), None) == _lib.FST_ERR_INVALID
+    assert "valid_rows" in _lib.last_error()
+
+
+def test_mask_lengths_read_back_the_valid_row_count():
+    import torch
+    from flash_spacetime import ops
+    lens = torch.tensor([5, 0, 8])
+    mask = torch.arange(8)[None, :] >= lens[:, None]  # True = padding
+    got, total = ops._mask_lengths(mask, True)
+    assert got.tolist() == [5, 0, 8] and total == 13
+    assert ops._mask_lengths(mask, False)[1] == 0  # unchecked: nothing read back
+    floats = torch.zeros(3, 8).masked_fill(mask, float("-inf"))
+    assert ops._mask_lengths(floats, True)[1] == 13
+    mask[0, 1] = True  # a hole inside event 0
+    with pytest.raises(ValueError, match="prefix"):
+        ops._mask_lengths(mask, True)
+    seq, hint = ops._padded_lengths(None, None, 3, 8, torch.device("cpu"), True, 20)
+    assert hint == 20 and seq.tolist() == [8, 8, 8]
+    with pytest.raises(ValueError, match="valid_rows"):
+        ops._padded_lengths(lens, None, 3, 8, torch.device("cpu"), True, -2)

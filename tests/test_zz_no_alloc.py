@@ -7,7 +7,8 @@ calls both entry points through ctypes on the same inputs, twice in a row
 (the built-in array keeps the previous call's contents), for a packed batch
 (whose tile prefix lives in that scratch) and a padded one, and requires the
 outputs and LSE to match the workspace-based entry point bitwise -- it is the
-same kernel on the same inputs. It also checks that an oversized batch is
+same kernel on the same inputs -- also for a padded batch with a valid row
+count, whose tile list holds two prefixes. It also checks that an oversized batch is
 rejected, that fp32 inputs (which need no scratch) are not limited by it, and,
 with a second GPU, that the per-device lookup serves that device. This file is
 named to be collected last.
@@ -72,6 +73,20 @@ def test_noalloc_padded_matches_forward():
     q, k, v = (case[x].to("cuda", torch.bfloat16) for x in ("q", "k", "v"))
     pb = _Problem(q, case["feats"].cuda(), case["weight"].cuda(), case["bias"].cuda(),
                   case["seqlens"].cuda(), None, None, True, True)
+    (ref_out, ref_lse), results = _run_both(pb, q, k, v)
+    for out, lse in results:
+        assert torch.equal(out, ref_out)
+        assert torch.equal(lse, ref_lse)
+
+
+def test_noalloc_padded_valid_rows_matches_forward():
+    # Host lengths give the problem its valid row count: the tile list and the
+    # padding-row prefix then live in the built-in scratch.
+    case = cs.padded_case(3, 70, 12, 32, 16, True, seed=407)
+    q, k, v = (case[x].to("cuda", torch.bfloat16) for x in ("q", "k", "v"))
+    pb = _Problem(q, case["feats"].cuda(), case["weight"].cuda(), case["bias"].cuda(),
+                  case["seqlens"], None, None, True, True)
+    assert 0 < pb.valid_rows < pb.rows
     (ref_out, ref_lse), results = _run_both(pb, q, k, v)
     for out, lse in results:
         assert torch.equal(out, ref_out)

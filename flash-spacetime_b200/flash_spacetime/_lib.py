@@ -29,6 +29,7 @@ EXPORTED = (
     "fst_forward_workspace_size",
     "fst_backward_workspace_size",
     "fst_dw_partial_count",
+    "fst_sum_partials",
     "fst_forward",
     "fst_backward",
     "fst_forward_noalloc",
@@ -128,6 +129,10 @@ def load() -> ctypes.CDLL:
         lib.fst_backward_workspace_size.argtypes = [ctypes.POINTER(FstProblem)]
         lib.fst_dw_partial_count.restype = ctypes.c_int64
         lib.fst_dw_partial_count.argtypes = [ctypes.POINTER(FstProblem)]
+        lib.fst_sum_partials.restype = ctypes.c_int
+        lib.fst_sum_partials.argtypes = [ctypes.POINTER(FstProblem), ctypes.c_void_p,
+                                         ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p,
+                                         ctypes.c_void_p]
         lib.fst_forward.restype = ctypes.c_int
         lib.fst_forward.argtypes = [ctypes.POINTER(FstForwardArgs), ctypes.c_void_p]
         lib.fst_backward.restype = ctypes.c_int

@@ -347,7 +347,7 @@ def fused_backward(
     want_absmax: bool = False,
     dqkv: Optional[Tensor] = None,
 ) -> Dict[str, Optional[Tensor]]:
-    """One ``fst_backward`` call plus the two deterministic host reductions.
+    """One ``fst_backward`` call plus the fixed-order sums of its dW / db partials.
 
     Returns dq, dk, dv (input dtype), dW ``[Dh, C]`` and db ``[Dh]`` (fp32,
     or None when the projection is unused), and the per-row diagnostics
@@ -385,15 +385,21 @@ def fused_backward(
                      pb.device)
     _lib.check(rc, "fst_backward")
 
+    # dW and db: the partials summed on the device in a fixed order (one
+    # launch; upstream sums on the host side of backward.py:607-622).
     dw = db = None
     if pb.attn or pb.act:
-        dw = dw_part[:nparts].sum(0)
-    if pb.b32 is not None:
-        if pb.act:
-            db = db_part[:nparts].sum(0)  # sum of dO over valid rows (backward.py:615-618)
-        else:
-            # The logit path's db vanishes analytically (backward.py:619-622).
-            db = torch.zeros(pb.dim, dtype=torch.float32, device=pb.device)
+        dw = torch.empty(pb.dim, pb.channels, dtype=torch.float32, device=pb.device)
+    if pb.b32 is not None and pb.act:
+        db = torch.empty(pb.dim, dtype=torch.float32, device=pb.device)  # sum of dO, valid rows
+    if dw is not None or db is not None:
+        rc = _timed_call("fst_sum_partials", lib.fst_sum_partials,
+                         (ctypes.byref(a.prob), _ptr(dw_part), _ptr(db_part), _ptr(dw), _ptr(db),
+                          _stream(pb.device)), pb.device)
+        _lib.check(rc, "fst_sum_partials")
+    if pb.b32 is not None and not pb.act:
+        # The logit path's db vanishes analytically (backward.py:619-622).
+        db = torch.zeros(pb.dim, dtype=torch.float32, device=pb.device)
     return {"dq": dq, "dk": dk, "dv": dv, "dW": dw, "db": db,
             "delta": delta, "sigma": sigma, "ds_absmax": absmax}
 

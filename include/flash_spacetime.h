@@ -155,8 +155,8 @@ typedef struct FstBackwardArgs {
   void* dq;              /* outputs, layout/dtype of q                       */
   void* dk;
   void* dv;
-  float* dw_partial;     /* [fst_dw_partial_count(), Dh, C] fp32; the caller */
-                         /* sums axis 0 (fixed order) to obtain dW           */
+  float* dw_partial;     /* [fst_dw_partial_count(), Dh, C] fp32; summed over */
+                         /* axis 0 in a fixed order (fst_sum_partials) -> dW */
   float* db_partial;     /* [fst_dw_partial_count(), Dh] fp32: partial sums  */
                          /* of dout over valid rows (db when act and bias)   */
   float* delta;          /* [rows, H] fp32: D_i = sum P dP / sum P, dP taken */
@@ -176,6 +176,15 @@ size_t fst_backward_workspace_size(const FstProblem* prob);
 
 /* Rows of dw_partial fst_backward writes for this problem. */
 int64_t fst_dw_partial_count(const FstProblem* prob);
+
+/* dW and db from fst_backward's partials, on the device in a fixed order:
+ * dw[i] = sum over r < fst_dw_partial_count(prob) of dw_partial[r][i]
+ * (i < Dh*C), db likewise over [Dh]. Either output may be NULL. The order of
+ * the additions depends only on the problem, so the sums are bitwise
+ * reproducible. Stream-ordered after the fst_backward call; one launch.
+ * Replaces the host-side sums of upstream's backward (backward.py:607-622). */
+int fst_sum_partials(const FstProblem* prob, const float* dw_partial, const float* db_partial,
+                     float* dw, float* db, void* stream);
 
 /* Fused forward (upstream forward.py:222-346). */
 int fst_forward(const FstForwardArgs* args, void* stream);

@@ -15,6 +15,7 @@
 #include <cstdint>
 #include <initializer_list>
 
+#include "fst_common.cuh"
 #include "fst_internal.h"
 
 namespace fst {
@@ -64,8 +65,15 @@ int check_problem(const FstProblem* p) {
       return fail(FST_ERR_INVALID, "padded total_rows must equal B*L");
   }
   if (p->valid_rows < 0) return fail(FST_ERR_INVALID, "negative valid_rows");
-  if (p->flags & ~FST_FLAG_SHARE_SMS)
+  if (p->flags & ~(FST_FLAG_SHARE_SMS | FST_FLAG_LONGEST_FIRST))
     return fail(FST_ERR_INVALID, "unknown flags 0x%x", (unsigned)p->flags);
+  if (p->flags & FST_FLAG_LONGEST_FIRST) {
+    if (p->event_order)
+      return fail(FST_ERR_INVALID, "FST_FLAG_LONGEST_FIRST needs event_order = NULL");
+    if (p->batch > fst::kMaxSelfOrdered)
+      return fail(FST_ERR_INVALID, "FST_FLAG_LONGEST_FIRST: %d events, at most %d (pass an "
+                  "event_order instead)", p->batch, fst::kMaxSelfOrdered);
+  }
   if (p->qkv_row_stride) {
     if (p->packed == 0)
       return fail(FST_ERR_INVALID,

@@ -76,10 +76,20 @@ __host__ __device__ __forceinline__ int pad_ctas(const FstProblem& p, int row_by
   const int64_t z = bytes >> 22;
   return z < 1 ? 1 : (z > 32 ? 32 : (int)z);
 }
-// Ints of the tile-list workspace: the tile prefix [B + 1], then, for a
-// padded layout, the padding-row prefix [B + 1].
-__host__ __device__ __forceinline__ int64_t tile_list_ints(const FstProblem& p) {
+// Whether the library ranks the events longest first itself
+// (FST_FLAG_LONGEST_FIRST, at most kMaxSelfOrdered events) into the workspace.
+constexpr int kMaxSelfOrdered = 1024;
+__host__ __device__ __forceinline__ bool self_ordered(const FstProblem& p) {
+  return (p.flags & FST_FLAG_LONGEST_FIRST) && !p.event_order && p.batch > 0;
+}
+// The tile-list workspace, in int32s: the tile prefix [B + 1]; for a padded
+// layout walked by the list, the padding-row prefix [B + 1]; for a
+// self-ordered problem, the event order [B] (order_offset).
+__host__ __device__ __forceinline__ int64_t order_offset(const FstProblem& p) {
   return (int64_t)(p.batch + 1) * (list_padding(p) ? 2 : 1);
+}
+__host__ __device__ __forceinline__ int64_t tile_list_ints(const FstProblem& p) {
+  return order_offset(p) + (self_ordered(p) ? p.batch : 0);
 }
 
 // Where one event lives. `row0` is the flat row of the event's first token in

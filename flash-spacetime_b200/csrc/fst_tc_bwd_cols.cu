@@ -672,16 +672,19 @@ static int launch_cols_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
       grid = dim3((p.max_len + S::BK - 1) / S::BK, p.batch, groups);
     }
     if (grid.x == 0 || grid.y == 0) return FST_OK;
+    // A self-ordered problem's event order, ranked by the row kernel's launch.
+    FstBackwardArgs ka = a;
+    if (self_ordered(p)) ka.prob.event_order = tile_start + order_offset(p);
     if constexpr (has_shared_variant<DH, C>()) {
       if (shared) {
         bwd_cols_tc_shared_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
-            a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
+            ka, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
         count_launch();
         return FST_OK;
       }
     }
     bwd_cols_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
-        a, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
+        ka, tile_start, per_group, (const T*)gu, (const T*)gwt, (const T*)gqt);
     count_launch();
     return FST_OK;
   }

@@ -1136,10 +1136,14 @@ static int launch_rows_shape(const FstBackwardArgs& a, cudaStream_t st, int* til
   const int groups = (int)grid.z;
   const int per_group = (p.heads + groups - 1) / groups;
   const int threads = (per_group + S::NE) * 32;
-  if (uses_tile_list(p)) tile_prefix(p, S::BM, tile_start, st);
+  // The tile list (and a self-ordered problem's event order, which the
+  // kernels then read) for this kernel and the column kernel after it.
+  if (uses_tile_list(p) || self_ordered(p)) tile_prefix(p, S::BM, tile_start, st);
+  FstBackwardArgs ka = a;
+  if (self_ordered(p)) ka.prob.event_order = tile_start + order_offset(p);
   if (grid.x == 0 || grid.y == 0) return FST_OK;
   bwd_rows_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(
-      a, tile_start, per_group, (T*)u_ws, (T*)wt_ws, (T*)qt_ws, maps);
+      ka, tile_start, per_group, (T*)u_ws, (T*)wt_ws, (T*)qt_ws, maps);
   count_launch();
   return FST_OK;
 }

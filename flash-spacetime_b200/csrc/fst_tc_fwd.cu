@@ -881,29 +881,53 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
 
 // ---------------------------------------------------------------------------
 
+__device__ __forceinline__ int event_len(const FstProblem& p, int b) {
+  return is_varlen(p) ? p.cu_seqlens[b + 1] - p.cu_seqlens[b]
+                      : min(max(p.seqlens[b], 0), p.max_len);
+}
+
 __global__ void tile_prefix_kernel(const FstProblem p, int bm, int* __restrict__ tile_start) {
   // Single-CTA exclusive scans over the events: of ceil(len_b / bm), the
   // events taken in p.event_order (position k holds event order[k]) or the
   // natural one, into tile_start[0..B]; for a padded layout walked by the
   // tile list, also of the padding row counts max_len - len_b in natural
   // order, into tile_start[B+1 .. 2B+1].
+  //
+  // A self-ordered problem (FST_FLAG_LONGEST_FIRST, B <= kMaxSelfOrdered)
+  // first ranks its events: the rank of event i is the number of events
+  // longer than it plus the number of equally long ones before it (a stable
+  // longest-first sort by counting, B^2 / 1024 comparisons a thread), and
+  // order[rank] = i goes to tile_start[order_offset ..] for the kernels.
   __shared__ int2 warp_sums[32];
   __shared__ int2 carry;
+  __shared__ int s_len[kMaxSelfOrdered];
+  __shared__ int s_ord[kMaxSelfOrdered];
   const bool pad = list_padding(p);
   const int batch = p.batch;
+  const bool ranked = self_ordered(p);
+  if (ranked) {
+    for (int i = threadIdx.x; i < batch; i += blockDim.x) s_len[i] = event_len(p, i);
+    __syncthreads();
+    int* order = tile_start + order_offset(p);
+    for (int i = threadIdx.x; i < batch; i += blockDim.x) {
+      const int li = s_len[i];
+      int rank = 0;
+      for (int j = 0; j < batch; ++j) {
+        const int lj = s_len[j];
+        rank += (lj > li) || (lj == li && j < i);
+      }
+      s_ord[rank] = i;
+      order[rank] = i;
+    }
+  }
   if (threadIdx.x == 0) carry = make_int2(0, 0);
   __syncthreads();
   for (int base = 0; base < batch; base += blockDim.x) {
     const int k = base + threadIdx.x;
     int2 v = make_int2(0, 0);
     if (k < batch) {
-      const int ev = p.event_order ? p.event_order[k] : k;
-      int len;
-      if (is_varlen(p)) {
-        len = p.cu_seqlens[ev + 1] - p.cu_seqlens[ev];
-      } else {
-        len = min(max(p.seqlens[ev], 0), p.max_len);
-      }
+      const int ev = ranked ? s_ord[k] : (p.event_order ? p.event_order[k] : k);
+      const int len = event_len(p, ev);
       v.x = (len + bm - 1) / bm;
       if (pad) v.y = p.max_len - min(max(p.seqlens[k], 0), p.max_len);
     }
@@ -972,7 +996,11 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
   const int groups = (p.heads + S::HP - 1) / S::HP;
   const int per_group = (p.heads + groups - 1) / groups;  // balanced, <= HP
   const int threads = (per_group + S::NE) * 32;
+  // A self-ordered problem's kernels read the order tile_prefix ranks.
+  FstForwardArgs ka = a;
+  if (self_ordered(p)) ka.prob.event_order = tile_start + order_offset(p);
   dim3 grid;
+  if (self_ordered(p) && !uses_tile_list(p)) tile_prefix(p, S::BM, tile_start, st);
   if (uses_tile_list(p)) {
     tile_prefix(p, S::BM, tile_start, st);
     const int64_t upper = (list_rows(p) + S::BM - 1) / S::BM + p.batch +
@@ -982,7 +1010,7 @@ static int launch_fwd_shape(const FstForwardArgs& a, cudaStream_t st, int* tile_
     grid = dim3((p.max_len + S::BM - 1) / S::BM, p.batch, groups);
   }
   if (grid.x == 0 || grid.y == 0) return FST_OK;
-  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(a, tile_start, per_group, maps);
+  fwd_tc_kernel<T, DH, C><<<grid, threads, S::SMEM, st>>>(ka, tile_start, per_group, maps);
   count_launch();
   return FST_OK;
 }

@@ -23,6 +23,8 @@ FST_ERR_DEVICE = 5
 
 ABI_VERSION = 5
 FST_FLAG_SHARE_SMS = 1  # FstProblem.flags: another kernel shares the SMs
+FST_FLAG_LONGEST_FIRST = 2  # FstProblem.flags: the library orders the events itself
+MAX_SELF_ORDERED = 1024  # events FST_FLAG_LONGEST_FIRST accepts
 
 EXPORTED = (
     "fst_abi_version",

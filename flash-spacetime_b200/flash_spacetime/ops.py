@@ -148,6 +148,16 @@ def _padded_lengths(seqlens: Any, mask: Optional[Tensor], batch: int, length: in
     return seqlens, hint
 
 
+def _event_order(lengths: Tensor) -> Optional[Tensor]:
+    """Longest-first event order (stable), or None when the library ranks the
+    events itself (FST_FLAG_LONGEST_FIRST, up to 1024 events: one ranking
+    step inside a kernel the call launches anyway, instead of a torch sort's
+    four launches)."""
+    if lengths.numel() <= _lib.MAX_SELF_ORDERED:
+        return None
+    return torch.argsort(lengths, descending=True, stable=True).to(torch.int32)
+
+
 class _Problem:
     """Shapes and host-side tensors of one call, in C-ABI form."""
 
@@ -189,8 +199,7 @@ class _Problem:
             length = 0
             self.seq = None
             # Longest events first (see the padded case below).
-            lens = self.cu[1:] - self.cu[:-1]
-            self.order = torch.argsort(lens, descending=True, stable=True).to(torch.int32)
+            self.order = _event_order(self.cu[1:] - self.cu[:-1])
             rows = total
             if feats.dim() != 2 or feats.shape[0] != total:
                 raise ValueError(f"varlen feats must be [T, F], got {tuple(feats.shape)}")
@@ -223,7 +232,7 @@ class _Problem:
             # Longest events first: their row / key blocks are scheduled
             # before the short ones', which balances the SMs (the results
             # do not depend on the order; the sort is stable).
-            self.order = torch.argsort(self.seq, descending=True, stable=True).to(torch.int32)
+            self.order = _event_order(self.seq)
             if feats.dim() != 3 or feats.shape[:2] != (batch, length):
                 raise ValueError(f"feats must be [B, L, F], got {tuple(feats.shape)}")
         if feats.shape[-1] < 4:
@@ -280,7 +289,8 @@ class _Problem:
         p.bias = _ptr(self.b32)
         p.event_order = _ptr(self.order)
         p.qkv_row_stride = self.qkv_row_stride
-        p.flags = _lib.FST_FLAG_SHARE_SMS if self.share_sms else 0
+        p.flags = (_lib.FST_FLAG_SHARE_SMS if self.share_sms else 0) | \
+            (_lib.FST_FLAG_LONGEST_FIRST if self.order is None else 0)
         p.valid_rows = self.valid_rows
         return p
 

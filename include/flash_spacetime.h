@@ -93,7 +93,8 @@ typedef struct FstProblem {
   const float* bias;         /* [Dh] device fp32, or NULL                     */
   /* Optional [B] device permutation of the events: the order in which the
    * kernels' row / key blocks are scheduled (longest first balances the SMs);
-   * NULL = natural order. Results do not depend on it. No upstream
+   * NULL = natural order, or the library's own longest-first order with
+   * FST_FLAG_LONGEST_FIRST. Results do not depend on it. No upstream
    * counterpart. */
   const int32_t* event_order;
   /* Elements between consecutive rows of q, k, v and of dq, dk, dv in the
@@ -127,6 +128,12 @@ typedef struct FstProblem {
  * two); about 7 % slower when nothing runs beside it. No upstream
  * counterpart. */
 #define FST_FLAG_SHARE_SMS 1
+
+/* The library puts the events in longest-first order itself (stable: equal
+ * lengths keep their index order), as an event_order would; event_order must
+ * then be NULL, and the batch at most 1024 events. One small kernel per call
+ * ranks the lengths; no host synchronisation. No upstream counterpart. */
+#define FST_FLAG_LONGEST_FIRST 2
 
 typedef struct FstForwardArgs {
   FstProblem prob;

@@ -179,3 +179,26 @@ def test_mask_lengths_read_back_the_valid_row_count():
     assert hint == 20 and seq.tolist() == [8, 8, 8]
     with pytest.raises(ValueError, match="valid_rows"):
         ops._padded_lengths(lens, None, 3, 8, torch.device("cpu"), True, -2)
+
+
+def test_longest_first_flag_is_checked():
+    # The library ranks at most 1024 events itself, and only when no
+    # event_order is given.
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.packed, p.batch, p.heads, p.max_len = 1, 0, 1025, 12, 64
+    p.head_dim, p.channels, p.feat_stride, p.total_rows = 32, 16, 4, 1025 * 64
+    p.seqlens = p.feats = p.freqs = 256  # never dereferenced by these calls
+    p.flags = _lib.FST_FLAG_LONGEST_FIRST
+    a = _lib.FstForwardArgs()
+    a.prob = p
+    assert lib.fst_forward(ctypes.byref(a), None) == _lib.FST_ERR_INVALID
+    assert "1024" in _lib.last_error()
+    a.prob.batch, a.prob.total_rows, a.prob.event_order = 8, 8 * 64, 256
+    assert lib.fst_forward(ctypes.byref(a), None) == _lib.FST_ERR_INVALID
+    assert "event_order" in _lib.last_error()
+    # Accepted: its workspace holds the ranked order after the tile prefix.
+    a.prob.event_order = None
+    assert lib.fst_forward_workspace_size(ctypes.byref(a.prob)) == (9 * 4 + 8 * 4 + 15) // 16 * 16
+    a.prob.flags = 4
+    assert lib.fst_forward(ctypes.byref(a), None) == _lib.FST_ERR_INVALID

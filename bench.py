@@ -538,6 +538,12 @@ def run_ours(args):
                                 f"{data['q'].numel() * data['q'].element_size() / 1e6:.0f} MB "
                                 f"each)"},
         "fwd_ms": fwd_ms, "bwd_ms": bwd_ms, "gather_ms": gather_ms, "peak_gib": peak_gib,
+        # Per valid (query, key) pair, as the kernels evaluate them: each of
+        # the three kernels (forward, row, column) forms E_ij once for all
+        # heads (C/2 sin + C/2 cos after one shared range reduction) and the
+        # interval's sqrt once, and one exp2 per head.
+        "transcendentals_per_pair": {"sin_cos": 3 * channels, "sqrt": 3, "exp2": 3 * heads,
+                                     "total": 3 * (channels + 1 + heads)},
         "roofline": {"bound": "tensor", "kernel": dom, "achieved": achieved,
                      "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                      "frac": achieved / peaks["bf16_tflops"], "traffic": traffic,

@@ -354,7 +354,7 @@ def run_ours(args):
         dist.init_process_group("nccl", device_id=device,
                                 timeout=__import__("datetime").timedelta(seconds=120))
     from flash_spacetime import _lib, ops, synthetic
-    from flash_spacetime.sharding import RowGather, max_over_ranks, ordered_sum
+    from flash_spacetime.sharding import RowGather, gather_over_ranks, ordered_sum
 
     lens, padlen, n_events, per_rank = _workload_lengths(args.workload, world, rank, args.seed,
                                                          args.events)
@@ -471,7 +471,9 @@ def run_ours(args):
     clk = clocks.stop(wall0, wall1)
     launches = lib.fst_kernel_launches() - launches0
     ms_local = ev0.elapsed_time(ev1) / args.steps
-    ms = max_over_ranks(ms_local, device)
+    rank_ms = gather_over_ranks(ms_local, device)  # every rank's step time
+    ms = max(rank_ms)
+    loads = [sum(n * n for n in x) for x in per_rank]
     peak_gib = (torch.cuda.max_memory_allocated(device) - base_mem) / 2**30
     ops.set_kernel_timer(None)
 
@@ -553,6 +555,11 @@ def run_ours(args):
         "clocks": clk,
         "e2e": e2e,
         "gpu_launches": launches,
+        # Per-rank device step times and the partition's balance of valid
+        # pairs (the sharding key): the job's time is the slowest rank's.
+        "ranks": {"ms_min": min(rank_ms), "ms_max": max(rank_ms),
+                  "ms_mean": sum(rank_ms) / len(rank_ms),
+                  "pairs_max_over_mean": max(loads) / (sum(loads) / len(loads))},
     }
     print(json.dumps(line), flush=True)
 

@@ -118,6 +118,19 @@ class RowGather:
         return (len(self.sizes) - 1) * self.send.numel() * self.send.element_size()
 
 
+def gather_over_ranks(value: float, device: torch.device,
+                      group: Optional[dist.ProcessGroup] = None) -> List[float]:
+    """Every rank's value of a per-rank scalar, in rank order (one all-gather):
+    the per-rank step times, whose maximum is the job's and whose spread is
+    the partition's imbalance."""
+    if not dist.is_initialized() or dist.get_world_size(group) == 1:
+        return [float(value)]
+    t = torch.tensor([float(value)], dtype=torch.float64, device=device)
+    out = torch.empty(dist.get_world_size(group), dtype=torch.float64, device=device)
+    dist.all_gather_into_tensor(out, t, group=group)
+    return [float(x) for x in out.tolist()]
+
+
 def max_over_ranks(value: float, device: torch.device,
                    group: Optional[dist.ProcessGroup] = None) -> float:
     """Maximum of a per-rank scalar (e.g. a device-timed duration)."""

@@ -10,6 +10,7 @@ import torch.distributed as dist
 import torch.multiprocessing as mp
 
 from flash_spacetime.sharding import (
+    gather_over_ranks,
     gather_rows,
     lpt_partition,
     max_over_ranks,
@@ -57,6 +58,7 @@ def _worker(rank, world, port, q):
         rows2 = gather_rows(torch.full((rank + 2, 3), float(rank)), sizes=[2, 3])
         assert [r.tolist() for r in rows2] == [r.tolist() for r in rows]
         m = max_over_ranks(float(rank) * 1.5, torch.device("cpu"))
+        assert gather_over_ranks(float(rank) * 1.5, torch.device("cpu")) == [0.0, 1.5]
         q.put((rank, s.tolist(), [r.tolist() for r in rows], m))
     finally:
         dist.destroy_process_group()

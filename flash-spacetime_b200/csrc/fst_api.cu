@@ -169,6 +169,18 @@ int64_t fst_dw_partial_count(const FstProblem* prob) {
                                        : fst::simt::dw_parts(*prob);
 }
 
+int fst_sum_partials(const FstProblem* prob, const float* dw_partial, const float* db_partial,
+                     float* dw, float* db, void* stream) {
+  const int rc = check_problem(prob);
+  if (rc) return rc;
+  const int64_t rows = fst_dw_partial_count(prob);
+  if (rows > 0 && ((dw && !dw_partial) || (db && !db_partial)))
+    return fail(FST_ERR_INVALID, "sum_partials: null partials");
+  if (!dw && !db) return FST_OK;
+  return fst::launch_sum_partials(dw_partial, db_partial, rows, prob->head_dim * prob->channels,
+                                  prob->head_dim, dw, db, (cudaStream_t)stream);
+}
+
 int fst_forward(const FstForwardArgs* a, void* stream) {
   if (!a) return fail(FST_ERR_INVALID, "null args");
   int rc = check_problem(&a->prob);

@@ -17,6 +17,10 @@ int api_fail(int code, const char* fmt, ...);
 // Raises `fn`'s dynamic shared memory limit to `bytes` on the current device,
 // once per device (bit d of `done`); returns 0 or a cudaError_t.
 int allow_dynamic_smem(const void* fn, int bytes, std::atomic<uint64_t>& done);
+// fst_sum_partials after validation: one launch summing `rows` partial rows
+// of ncw dW and ncb db columns in a fixed order (NULL outputs skipped).
+int launch_sum_partials(const float* dw_partial, const float* db_partial, int64_t rows, int ncw,
+                        int ncb, float* dw, float* db, cudaStream_t st);
 namespace simt {
 int launch_fwd(const FstForwardArgs& a, cudaStream_t st);
 int launch_bwd(const FstBackwardArgs& a, cudaStream_t st);

@@ -75,25 +75,16 @@ __global__ void __cluster_dims__(1, kSplit, 1) __launch_bounds__(kWarps * 32)
 }
 
 }  // namespace
-}  // namespace fst
 
-extern "C" int fst_sum_partials(const FstProblem* prob, const float* dw_partial,
-                                const float* db_partial, float* dw, float* db, void* stream) {
-  if (!prob) return fst::api_fail(FST_ERR_INVALID, "fst_sum_partials: null problem");
-  const int64_t rows = fst_dw_partial_count(prob);
-  const int ncw = prob->head_dim * prob->channels, ncb = prob->head_dim;
-  if (ncw <= 0 || ncb <= 0)
-    return fst::api_fail(FST_ERR_INVALID, "fst_sum_partials: bad sizes Dh=%d C=%d",
-                         prob->head_dim, prob->channels);
-  if ((dw && rows > 0 && !dw_partial) || (db && rows > 0 && !db_partial))
-    return fst::api_fail(FST_ERR_INVALID, "fst_sum_partials: null partials");
-  if (!dw && !db) return FST_OK;
-  const dim3 grid((ncw + 31) / 32 + (ncb + 31) / 32, fst::kSplit);
-  fst::sum_partials_kernel<<<grid, fst::kWarps * 32, 0, (cudaStream_t)stream>>>(
-      dw_partial, db_partial, rows, ncw, ncb, dw, db);
+int launch_sum_partials(const float* dw_partial, const float* db_partial, int64_t rows, int ncw,
+                        int ncb, float* dw, float* db, cudaStream_t st) {
+  const dim3 grid((ncw + 31) / 32 + (ncb + 31) / 32, kSplit);
+  sum_partials_kernel<<<grid, kWarps * 32, 0, st>>>(dw_partial, db_partial, rows, ncw, ncb, dw,
+                                                      db);
   const cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess)
-    return fst::api_fail(FST_ERR_CUDA, "fst_sum_partials: launch: %s", cudaGetErrorString(err));
-  fst::count_launch();
+    return api_fail(FST_ERR_CUDA, "sum_partials: launch: %s", cudaGetErrorString(err));
+  count_launch();
   return FST_OK;
 }
+}  // namespace fst

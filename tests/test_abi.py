@@ -202,3 +202,21 @@ def test_longest_first_flag_is_checked():
     assert lib.fst_forward_workspace_size(ctypes.byref(a.prob)) == (9 * 4 + 8 * 4 + 15) // 16 * 16
     a.prob.flags = 4
     assert lib.fst_forward(ctypes.byref(a), None) == _lib.FST_ERR_INVALID
+
+
+def test_sum_partials_checks_its_problem():
+    # An invalid problem is refused (it would otherwise count no partials and
+    # write zeros), and so are missing partials for a requested output.
+    lib = _lib.load()
+    p = _lib.FstProblem()
+    p.dtype, p.batch, p.heads, p.head_dim, p.channels = 1, 1, 1, 32, 15  # odd C
+    p.feat_stride = 4
+    assert lib.fst_sum_partials(ctypes.byref(p), None, None, 256, 256, None) == \
+        _lib.FST_ERR_INVALID
+    p.channels, p.packed, p.max_len, p.total_rows = 16, 0, 64, 64
+    p.seqlens = p.feats = p.freqs = 256  # never dereferenced by these calls
+    assert lib.fst_dw_partial_count(ctypes.byref(p)) > 0
+    assert lib.fst_sum_partials(ctypes.byref(p), None, None, 256, None, None) == \
+        _lib.FST_ERR_INVALID
+    assert "partials" in _lib.last_error()
+    assert lib.fst_sum_partials(ctypes.byref(p), None, None, None, None, None) == _lib.FST_OK

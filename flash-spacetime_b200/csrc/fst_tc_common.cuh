@@ -425,10 +425,10 @@ __device__ __forceinline__ void fill_rows(T* __restrict__ base, const EventSpan&
 }
 
 // A padded layout walked by the tile list has no CTA past an event's end, so
-// the padding rows [len_b, max_len) of all events are split evenly over the
-// first n CTAs of the list (pad_start: the exclusive prefix of max_len - len_b
-// in natural event order, written by tile_prefix). CTA t calls fn(b, r0, r1)
-// for each row range of its share -- one or a few, in ascending rows.
+// the padding rows [len_b, max_len) of all events are split evenly into n
+// shares (pad_start: the exclusive prefix of max_len - len_b in natural event
+// order, written by tile_prefix). For share t, fn(b, r0, r1) is called for
+// each row range it holds -- one or a few, in ascending rows.
 template <typename F>
 __device__ __forceinline__ void padding_share(const FstProblem& p,
                                               const int* __restrict__ pad_start, int t, int n,

@@ -505,7 +505,13 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         fv[g][r] = fr[g][r] * 0.15915494309189535f;
       }
     }
-    const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
+    // Each lane of a quad forms the interval angle of one (query, 8-key
+    // tile) pair of the warp's QPE (<= 2) queries and the chunk's two key
+    // tiles: lane m4 takes query m4 % QPE and tile m4 / QPE % 2, and the
+    // others read it by shuffle (no angle is formed twice).
+    static_assert(S::QPE <= 2, "one angle per lane");
+    const int my_t = m4 % S::QPE, my_nt = (m4 / S::QPE) & 1;
+    const int qx_row = qe + my_t;
     Coord4 cq;
     cq.x = fQC[qx_row * 4 + 0];
     cq.y = fQC[qx_row * 4 + 1];
@@ -543,17 +549,16 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
     auto produce = [&](int n, int s, EFrag& eb) {
       cp_async_wait<1>();
       __syncwarp();
-      float xl[2];
-#pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
+      float x1;
+      {
         const float4 ck =
-            *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + nt * 8 + r8) * 16);
+            *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + my_nt * 8 + r8) * 16);
         Coord4 c4;
         c4.x = ck.x;
         c4.y = ck.y;
         c4.z = ck.z;
         c4.t = ck.w;
-        xl[nt] = pair_angle_fast(cq, c4);
+        x1 = pair_angle_fast(cq, c4);
       }
       __syncwarp();
       load_coords(n + 2);
@@ -564,7 +569,7 @@ __global__ void __launch_bounds__(RowShape<DH, C>::NWARPS * 32, 1)
         float sn[2][S::FG][2], cs[2][S::FG][2];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+          const float xt = __shfl_sync(0xffffffffu, x1, (lane & ~3) | (t + S::QPE * nt));
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
             sincos_xf2(xt, fr[g], fv[g], sn[nt][g], cs[nt][g]);

@@ -219,11 +219,18 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
         fv[g][r] = fr[g][r] * 0.15915494309189535f;
       }
     }
-    // Coordinates of the two keys this lane pairs with (n-tile 0 and 1).
+    // The interval angles of the warp's QPE queries and the two 8-key tiles:
+    // with QPE = 4 lane m4 of a quad forms query m4's angles for both tiles;
+    // with QPE <= 2 each lane forms one (query m4 % QPE, tile m4 / QPE % 2)
+    // angle, so that none is formed twice. The others read them by shuffle.
+    constexpr bool kOneAngle = S::QPE <= 2;
+    const int my_t = kOneAngle ? m4 % S::QPE : (m4 < S::QPE ? m4 : 0);
+    const int my_nt = kOneAngle ? (m4 / S::QPE) & 1 : 0;
+    // Coordinates of the keys this lane pairs with (both n-tiles, or my_nt).
     Coord4 ck[2];
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      const int j = nt * 8 + r8;
+    for (int nt = 0; nt < (kOneAngle ? 1 : 2); ++nt) {
+      const int j = (kOneAngle ? my_nt : nt) * 8 + r8;
       ck[nt].x = fKC[j * 4 + 0];
       ck[nt].y = fKC[j * 4 + 1];
       ck[nt].z = fKC[j * 4 + 2];
@@ -300,19 +307,18 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
           ldsm_x4(au, ua[t][ks]);
           ldsm_x4(aw, wa[t][ks]);
         }
-      // x for (query m4 of this warp, key nt*8 + r8).
+      // x for (query my_t of this warp, key nt*8 + r8): both tiles, or my_nt.
       float xl[2];
       {
-        const int t = m4 < S::QPE ? m4 : 0;
         const float4 c4 =
-            *(const float4*)(smem + S::OFF_ER + (e * 2 + s) * S::SZ_ER + 2 * S::UW + t * 16);
+            *(const float4*)(smem + S::OFF_ER + (e * 2 + s) * S::SZ_ER + 2 * S::UW + my_t * 16);
         Coord4 cq;
         cq.x = c4.x;
         cq.y = c4.y;
         cq.z = c4.z;
         cq.t = c4.w;
         xl[0] = pair_angle_fast(cq, ck[0]);
-        xl[1] = pair_angle_fast(cq, ck[1]);
+        if (!kOneAngle) xl[1] = pair_angle_fast(cq, ck[1]);
       }
       __syncwarp();
       load_ring(n + 2);
@@ -332,7 +338,9 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
           float sn[2][S::FG][2], cs[2][S::FG][2];
 #pragma unroll
           for (int nt = 0; nt < 2; ++nt) {
-            const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+            const float xt =
+                kOneAngle ? __shfl_sync(0xffffffffu, xl[0], (lane & ~3) | (t + S::QPE * nt))
+                          : __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
 #pragma unroll
             for (int g = 0; g < S::FG; ++g)
               sincos_xf2(xt, fr[g], fv[g], sn[nt][g], cs[nt][g]);

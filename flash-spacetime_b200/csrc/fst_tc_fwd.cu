@@ -341,8 +341,16 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         fv[g][r] = fr[g][r] * 0.15915494309189535f;
       }
     }
-    // Coordinates of the query this lane evaluates x for (lane group m4).
-    const int qx_row = qe + (m4 < S::QPE ? m4 : 0);
+    // The interval angles of the warp's QPE queries and the chunk's two
+    // 8-key tiles: with QPE = 4 lane m4 of a quad forms query m4's angles
+    // for both tiles; with QPE <= 2 (wide shapes) each lane forms one
+    // (query m4 % QPE, tile m4 / QPE % 2) angle, so that none is formed
+    // twice. The others read them by shuffle. (64, 64), whose forward
+    // already spills, measured 3 % slower with it and keeps both per lane.
+    constexpr bool kOneAngle = S::QPE <= 2 && DH * C < 64 * 64;
+    const int my_t = kOneAngle ? m4 % S::QPE : m4;
+    const int my_nt = kOneAngle ? (m4 / S::QPE) & 1 : 0;
+    const int qx_row = qe + my_t;
     Coord4 cq;
     cq.x = fQC[qx_row * 4 + 0];
     cq.y = fQC[qx_row * 4 + 1];
@@ -383,11 +391,12 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     auto produce = [&](int n, int s, EFrag& eb) {
       cp_async_wait<1>();
       __syncwarp();
-      // x for (query qx_row, key nt*8 + r8).
+      // x for (query qx_row, key nt*8 + r8): both tiles, or tile my_nt.
       float xl[2];
 #pragma unroll
-      for (int nt = 0; nt < 2; ++nt) {
-        const float4 ck = *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + nt * 8 + r8) * 16);
+      for (int nt = 0; nt < (kOneAngle ? 1 : 2); ++nt) {
+        const int kt = kOneAngle ? my_nt : nt;
+        const float4 ck = *(const float4*)(smem + S::OFF_C + (e * 2 * S::BN + s * S::BN + kt * 8 + r8) * 16);
         Coord4 c4;
         c4.x = ck.x;
         c4.y = ck.y;
@@ -403,7 +412,9 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
         float sn[2][S::FG][2], cs[2][S::FG][2];
 #pragma unroll
         for (int nt = 0; nt < 2; ++nt) {
-          const float xt = __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
+          const float xt =
+              kOneAngle ? __shfl_sync(0xffffffffu, xl[0], (lane & ~3) | (t + S::QPE * nt))
+                        : __shfl_sync(0xffffffffu, xl[nt], (lane & ~3) | t);
 #pragma unroll
           for (int g = 0; g < S::FG; ++g)
             sincos_xf2(xt, fr[g], fv[g], sn[nt][g], cs[nt][g]);

@@ -22,7 +22,7 @@ Under torchrun (N > 1) every rank owns a shard of the events chosen by
 longest-first L^2 balancing: N x 256 events for config1 (weak scaling:
 per-GPU work stays fixed), the fixed 2048 events of config4 (strong
 scaling). Inside the step the per-rank dW/db partials are gathered and
-summed in rank order; for config4 (and with ``--gather-out``) the outputs
+summed the same way on every rank; for config4 (and with ``--gather-out``) the outputs
 of all ranks are also all-gathered over NCCL after the backward (valid rows,
 packed), as the sharded long-event run specifies. The step time is the max
 over ranks of the device-timed duration.

@@ -118,12 +118,13 @@ __device__ __forceinline__ void bwd_cols_body(const FstBackwardArgs& a,
     int t = blockIdx.x;
     if (list_padding(p)) {
       const int writers = pad_ctas(p, DH * 4);  // padding bytes per (row, head)
-      t = list_padded_role(p, tile_start, S::BK, writers, [&](int e, int r0, int r1, int nan) {
+      auto fill = [&](int e, int r0, int r1, int nan) {
         const EventSpan es = qkv_span(p, e, DH);
         const uint32_t v2 = nan ? E::kNaN2 : 0u;
         fill_rows<T, DH>(gdk, es, nullptr, nullptr, es, r0, r1, h0, NH, v2, 0.f);
         fill_rows<T, DH>(gdv, es, nullptr, nullptr, es, r0, r1, h0, NH, v2, 0.f);
-      });
+      };
+      t = list_padded_role(p, tile_start, S::BK, writers, blockIdx.x, gridDim.x, fill);
       if (t < 0) return;
     }
     if (!list_tile(p, tile_start, t, b, kb)) return;

@@ -386,8 +386,9 @@ __device__ __forceinline__ void stage_rows(const T* __restrict__ src, const Even
 // Entry t of the tile list (tile_prefix: the exclusive prefix tile_start[0..B]
 // of each event's block count, events in p.event_order): its event b and the
 // block's index within the event. False past the list's end.
-__device__ __forceinline__ bool list_tile(const FstProblem& p, const int* __restrict__ tile_start,
-                                          int t, int& b, int& blk) {
+__host__ __device__ __forceinline__ bool list_tile(const FstProblem& p,
+                                                   const int* __restrict__ tile_start, int t,
+                                                   int& b, int& blk) {
   if (t >= tile_start[p.batch]) return false;
   int lo = 0, hi = p.batch - 1;
   while (lo < hi) {  // last position with tile_start[pos] <= t
@@ -428,11 +429,14 @@ __device__ __forceinline__ void fill_rows(T* __restrict__ base, const EventSpan&
 // the padding rows [len_b, max_len) of all events are split evenly into n
 // shares (pad_start: the exclusive prefix of max_len - len_b in natural event
 // order, written by tile_prefix). For share t, fn(b, r0, r1) is called for
-// each row range it holds -- one or a few, in ascending rows.
+// each row range it holds -- one or a few, in ascending rows. (Host-
+// callable, like list_tile and list_padded_role, so that a CPU test can check
+// the row arithmetic of the padding writers.)
+#pragma nv_exec_check_disable
 template <typename F>
-__device__ __forceinline__ void padding_share(const FstProblem& p,
-                                              const int* __restrict__ pad_start, int t, int n,
-                                              F&& fn) {
+__host__ __device__ __forceinline__ void padding_share(const FstProblem& p,
+                                                       const int* __restrict__ pad_start, int t,
+                                                       int n, F&& fn) {
   const int64_t total = pad_start[p.batch];
   int64_t r = total * t / n;
   const int64_t r1 = total * (t + 1) / n;
@@ -444,7 +448,7 @@ __device__ __forceinline__ void padding_share(const FstProblem& p,
   }
   for (int b = lo; b < p.batch && r < r1; ++b) {
     const int64_t s0 = pad_start[b];
-    const int64_t s1 = min(r1, (int64_t)pad_start[b + 1]);
+    const int64_t s1 = r1 < pad_start[b + 1] ? r1 : (int64_t)pad_start[b + 1];
     if (s1 <= r) continue;                                 // no padding rows in event b
     const int len = p.max_len - (pad_start[b + 1] - pad_start[b]);  // clamped seqlens[b]
     fn(b, len + (int)(r - s0), len + (int)(s1 - s0));
@@ -452,8 +456,9 @@ __device__ __forceinline__ void padding_share(const FstProblem& p,
   }
 }
 
-// Role of a CTA in a padded layout walked by the tile list (list_padding).
-// Such a grid is n_tiles live blocks after zc = gridDim.x - n_tiles CTAs.
+// Role of CTA t of a grid of g (blockIdx.x, gridDim.x) in a padded layout
+// walked by the tile list (list_padding). Such a grid is n_tiles live blocks
+// after zc = g - n_tiles CTAs.
 // The first nz = min(zc, writers) of those write the zero padding rows,
 // split evenly between them, while the live blocks run beside them
 // (`writers` = pad_ctas, which the launch adds to the grid); the others exit.
@@ -463,18 +468,19 @@ __device__ __forceinline__ void padding_share(const FstProblem& p,
 // row of the blocks t, t + g, ..., and returns kRolePoisoned. fill(b, r0, r1,
 // nan) writes rows [r0, r1) of event b: zeros, or NaN when nan != 0.
 constexpr int kRoleDone = -1, kRolePoisoned = -2;
+#pragma nv_exec_check_disable
 template <typename F>
-__device__ __forceinline__ int list_padded_role(const FstProblem& p,
-                                                const int* __restrict__ tile_start, int bm,
-                                                int writers, F&& fill) {
+__host__ __device__ __forceinline__ int list_padded_role(const FstProblem& p,
+                                                         const int* __restrict__ tile_start,
+                                                         int bm, int writers, int t, int g,
+                                                         F&& fill) {
   const int n_tiles = tile_start[p.batch];
-  const int g = gridDim.x, t = blockIdx.x;
   const int zc = g - n_tiles;
   const int* pad_start = tile_start + p.batch + 1;
   auto zero = [&](int b, int r0, int r1) { fill(b, r0, r1, 0); };
   if (zc >= 1) {
     if (t >= zc) return t - zc;
-    const int nz = min(zc, writers);
+    const int nz = zc < writers ? zc : writers;
     if (t < nz) padding_share(p, pad_start, t, nz, zero);
     return kRoleDone;
   }
@@ -482,8 +488,9 @@ __device__ __forceinline__ int list_padded_role(const FstProblem& p,
   for (int tt = t; tt < n_tiles; tt += g) {
     int b, blk;
     list_tile(p, tile_start, tt, b, blk);
-    const int len = min(max(p.seqlens[b], 0), p.max_len);
-    fill(b, blk * bm, min(len, (blk + 1) * bm), 1);
+    const int sl = p.seqlens[b] < 0 ? 0 : p.seqlens[b];
+    const int len = sl < p.max_len ? sl : p.max_len;
+    fill(b, blk * bm, len < (blk + 1) * bm ? len : (blk + 1) * bm, 1);
   }
   return kRolePoisoned;
 }

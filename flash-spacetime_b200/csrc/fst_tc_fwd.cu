@@ -162,11 +162,12 @@ __global__ void __launch_bounds__(FwdShape<DH, C>::NWARPS * 32, 1)
     int t = blockIdx.x;
     if (list_padding(p)) {
       const int writers = pad_ctas(p, DH * 2 + 4);  // padding bytes per (row, head)
-      t = list_padded_role(p, tile_start, S::BM, writers, [&](int e, int r0, int r1, int nan) {
+      auto fill = [&](int e, int r0, int r1, int nan) {
         const EventSpan es = event_span(p, e);
         fill_rows<T, DH>(gout, es, a.lse, nullptr, es, r0, r1, h0, NH, nan ? E::kNaN2 : 0u,
                          nan ? __int_as_float(0x7fc00000) : 0.f);
-      });
+      };
+      t = list_padded_role(p, tile_start, S::BM, writers, blockIdx.x, gridDim.x, fill);
       if (t < 0) return;
     }
     if (!list_tile(p, tile_start, t, b, qb)) return;
